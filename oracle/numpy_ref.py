@@ -1,0 +1,279 @@
+"""CPU restatement of the decode step's per-operator math (the reference's NumPy specification,
+harness/numpy_ref.py:36-321, plus the stock tasks it composes with: embedding, dense SwiGLU,
+combine, argmax).
+
+TEST INFRASTRUCTURE. This module is the checker the CUDA path is compared with; it is never the
+thing measured or shipped. Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s
+``cpu_baseline`` / ``--impl reference`` legs may import it.
+
+Rounding points are the reference's (BF16 wherever the reference stores BF16 or feeds a BF16
+matrix operand); the two freedoms the reference leaves open are closed as ``oracle.detmath``
+explains: every dot product is exact and rounded once, and exp/log are deterministic routines.
+So the CUDA kernels, which make the same choices, must agree bit for bit, and the reference's
+own functions agree within their own tolerances (tests/test_oracle_pins.py checks both).
+
+Array conventions: BF16 tensors are float32 arrays holding BF16 values (as numpy_ref does).
+"""
+import numpy as np
+
+from oracle.detmath import (F32, F64, bf16, bf16_from_f64, det_exp, det_log, dot_exact,
+                            f32_from_f64, silu, sum_f64)
+
+__all__ = ["bf16", "rmsnorm", "rope", "mla_prep", "mla_attend", "merge_partials", "mla_merge_uv",
+           "moe_router", "moe_router_norm", "moe_w13", "moe_w2", "silu", "linear", "linear_norm",
+           "linear_residual", "moe_combine", "dense_mlp", "embed", "lm_head_argmax",
+           "partials_row", "softmax_det"]
+
+
+def partials_row(d_c):
+    """Innermost width of the split-KV partials: d_c values of o, the lse at column d_c, padded
+    to a multiple of 4 floats (16-byte rows). The reference's layout: fleet/graph_plan.py:214-218."""
+    return ((d_c + 1 + 3) // 4) * 4
+
+
+# ---------------------------------------------------------------------------------------------
+# norms and rotary embedding
+
+
+def rmsnorm(x, w, eps=1e-6):
+    """DeepseekV2RMSNorm on BF16 inputs (numpy_ref.py:54-60; modeling_deepseek.py:94-108).
+    The sum of squares is exact (FP64), the mean rounded once to FP32; then FP32
+    1/sqrt(var + eps), the normalised value rounded to BF16, times the BF16 weight, rounded."""
+    x = np.asarray(x, F32)
+    n = x.shape[-1]
+    var = f32_from_f64(sum_f64(x.astype(F64) ** 2) / n)[..., None]
+    r = (F32(1.0) / np.sqrt((var + F32(eps)).astype(F32))).astype(F32)
+    xn = bf16((x * r).astype(F32))
+    return bf16((np.asarray(w, F32) * xn).astype(F32))
+
+
+def rope(x, cos_row, sin_row):
+    """apply_rotary_pos_emb on the last dim (numpy_ref.py:63-71; modeling_deepseek.py:339-372):
+    de-interleave (even, odd) pairs into two halves, then bf16(bf16(x cos) + bf16(rot sin)).
+    Each rounding follows one FP32 operation on BF16 values, so this is exact on any machine."""
+    x = np.asarray(x, F32)
+    d = x.shape[-1]
+    x = x.reshape(*x.shape[:-1], d // 2, 2).swapaxes(-1, -2).reshape(*x.shape[:-1], d)
+    h = d // 2
+    rot = np.concatenate([-x[..., h:], x[..., :h]], axis=-1)
+    return bf16(bf16((x * np.asarray(cos_row, F32)).astype(F32))
+                + bf16((rot * np.asarray(sin_row, F32)).astype(F32)))
+
+
+# ---------------------------------------------------------------------------------------------
+# linears (the batch-1 GEMVs)
+
+
+def linear(x, W):
+    """bf16(W x): exact products, one rounding (numpy_ref.py:304-307)."""
+    return bf16_from_f64(dot_exact(W, x))
+
+
+def linear_residual(x, W, res):
+    """bf16(W x + res), the residual added before the one rounding (numpy_ref.py:310-313)."""
+    return bf16_from_f64(dot_exact(W, x) + np.asarray(res, F64))
+
+
+def linear_norm(x, w_norm, W, eps=1e-6):
+    """rmsnorm prologue then the linear (numpy_ref.py:295-301). Returns (h, out)."""
+    h = rmsnorm(x, w_norm, eps)
+    return h, linear(h, W)
+
+
+# ---------------------------------------------------------------------------------------------
+# MLA
+
+
+def mla_prep(qkva, w_kv_norm, W_uk, cos_row, sin_row, *, nh=16, d_n=128, d_r=64, d_c=512,
+             eps=1e-6):
+    """One decode token (numpy_ref.py:85-103; mla_prep_mi300.cuh:34-139).
+    qkva [nh*(d_n+d_r) + d_c + d_r]; W_uk [nh, d_n, d_c]. Returns c_row [d_c], k_pe_row [d_r],
+    ql_nope [nh, d_c] = bf16(q_nope[h] @ W_uk[h]), q_pe [nh, d_r]."""
+    q_out = nh * (d_n + d_r)
+    qkva = np.asarray(qkva, F32)
+    q = qkva[:q_out].reshape(nh, d_n + d_r)
+    c_raw = qkva[q_out:q_out + d_c]
+    k_pe_raw = qkva[q_out + d_c:q_out + d_c + d_r]
+    c_row = rmsnorm(c_raw, w_kv_norm, eps)
+    k_pe_row = rope(k_pe_raw, cos_row, sin_row)
+    q_nope, q_pe = q[:, :d_n], q[:, d_n:]
+    q_pe = rope(q_pe, cos_row, sin_row)
+    ql = np.einsum("hn,hnc->hc", q_nope.astype(F64), np.asarray(W_uk, F64))
+    return c_row, k_pe_row, bf16_from_f64(ql), q_pe
+
+
+def mla_attend(ql_nope, q_pe, c_kv, k_pe, step, softmax_scale, *, split=32, n_splits=None,
+               debug_scores=False):
+    """Split-KV attention over cache rows [0, step] (numpy_ref.py:110-149).
+
+    Per split j (rows [j*split, min(j*split+split, step+1))) and head h:
+      s = f32(exact ql_nope.c_kv + q_pe.k_pe) * f32(scale)
+      m = max s;  p = det_exp(s - m);  l = f32(exact sum p)
+      o = f32(exact sum bf16(p) c_kv) / l;  lse = m + det_log(l)
+    An empty split stores o = 0 and lse = -inf. Returns partials [n_splits, nh, d_c + 1] FP32
+    (and the scaled scores [nh, step + 1] with debug_scores)."""
+    ql_nope = np.asarray(ql_nope, F64)
+    q_pe = np.asarray(q_pe, F64)
+    c_kv = np.asarray(c_kv, F32)
+    k_pe = np.asarray(k_pe, F32)
+    nh, d_c = ql_nope.shape
+    s_max = c_kv.shape[0]
+    n_splits = n_splits or -(-s_max // split)
+    partials = np.zeros((n_splits, nh, d_c + 1), F32)
+    scores_all = np.zeros((nh, step + 1), F32) if debug_scores else None
+    scale = F32(softmax_scale)
+    for j in range(n_splits):
+        lo, hi = j * split, min(j * split + split, step + 1)
+        if lo > step:
+            partials[j, :, d_c] = -np.inf
+            continue
+        s64 = ql_nope @ c_kv[lo:hi].astype(F64).T + q_pe @ k_pe[lo:hi].astype(F64).T
+        s = (f32_from_f64(s64) * scale).astype(F32)
+        if debug_scores:
+            scores_all[:, lo:hi] = s
+        m = s.max(axis=1)
+        p = det_exp((s - m[:, None]).astype(F32))
+        l = f32_from_f64(sum_f64(p, axis=1))
+        acc = bf16(p).astype(F64) @ c_kv[lo:hi].astype(F64)
+        partials[j, :, :d_c] = (f32_from_f64(acc) / l[:, None]).astype(F32)
+        partials[j, :, d_c] = (m + det_log(l)).astype(F32)
+    return (partials, scores_all) if debug_scores else partials
+
+
+def merge_partials(partials, step, *, split=32, d_c=None):
+    """Merge of the live splits (numpy_ref.py:152-165): M = max lse, w_j = det_exp(lse_j - M),
+    o = f32(exact sum w_j o_j / exact sum w_j). d_c: the logical width when rows are padded."""
+    if d_c is None:
+        d_c = partials.shape[2] - 1
+    live = -(-(step + 1) // split)
+    lse = np.asarray(partials[:live, :, d_c], F32)
+    M = lse.max(axis=0)
+    with np.errstate(invalid="ignore"):
+        w = det_exp((lse - M[None, :]).astype(F32))                    # [live, nh]
+    num = np.einsum("jh,jhc->hc", w.astype(F64), np.asarray(partials[:live, :, :d_c], F64))
+    den = np.sum(w.astype(F64), axis=0)
+    return f32_from_f64(num / den[:, None])
+
+
+def mla_merge_uv(partials, W_uv, step, *, split=32, d_c=None):
+    """attn [nh * d_v]: per head the merge, o rounded to BF16, then bf16(o[h] @ W_uv[h]^T)
+    (numpy_ref.py:168-174)."""
+    o = bf16(merge_partials(partials, step, split=split, d_c=d_c))
+    attn = np.einsum("hc,hvc->hv", o.astype(F64), np.asarray(W_uv, F64))
+    return bf16_from_f64(attn.reshape(-1))
+
+
+# ---------------------------------------------------------------------------------------------
+# MoE
+
+
+def softmax_det(logits):
+    """FP32 softmax with the deterministic exp: e = det_exp(l - max l), p = e / f32(exact sum e)."""
+    logits = np.asarray(logits, F32)
+    m = logits.max(axis=-1, keepdims=True)
+    e = det_exp((logits - m).astype(F32))
+    s = f32_from_f64(sum_f64(e, axis=-1))[..., None]
+    return (e / s).astype(F32)
+
+
+def moe_router(h, W_gate, *, topk=6, n_experts=64, forced=(64, 65), scaling=1.0, logit_bias=None):
+    """FP32 router with the shared experts forced in (numpy_ref.py:205-234;
+    moe_router_mi300.cuh:115-354; HF MoEGate modeling_deepseek.py:393-470).
+
+    logits = f32(exact W_gate h) (+ logit_bias, FP32, when given: the injected-routing case);
+    p = softmax; top-k by repeated argmax, ties to the lower index; topk_w = p * scaling, then
+    1.0 per forced expert; routing [E + n_forced] (slot + 1, else 0); mask [E + n_forced + 1]
+    (ids in slot order, -1 in unused entries, the count last)."""
+    logits = f32_from_f64(dot_exact(W_gate, h))
+    if logit_bias is not None:
+        logits = (logits + np.asarray(logit_bias, F32)).astype(F32)
+    p = softmax_det(logits)
+    idx = []
+    remaining = p.copy()
+    for _ in range(topk):
+        e = int(np.argmax(remaining))
+        idx.append(e)
+        remaining[e] = -np.inf
+    ids = idx + list(forced)
+    n_slots = topk + len(forced)
+    n_total = n_experts + len(forced)
+    topk_w = np.array([p[e] * F32(scaling) for e in idx] + [1.0] * len(forced), F32)
+    routing = np.zeros(n_total, np.int32)
+    for k, e in enumerate(ids):
+        routing[e] = k + 1
+    mask = np.full(n_total + 1, -1, np.int32)
+    mask[:n_slots] = ids
+    mask[n_total] = n_slots
+    return logits, topk_w, routing, mask
+
+
+def moe_router_norm(x_res, w_norm, W_gate, *, eps=1e-6, topk=6, n_experts=64, forced=(64, 65),
+                    scaling=1.0, logit_bias=None):
+    """The router with the post-attention norm folded in (numpy_ref.py:237-245).
+    Returns (h, logits, topk_w, routing, mask)."""
+    h = rmsnorm(x_res, w_norm, eps)
+    return (h,) + moe_router(h, W_gate, topk=topk, n_experts=n_experts, forced=forced,
+                             scaling=scaling, logit_bias=logit_bias)
+
+
+def moe_w13(h, W13, mask, n_slots=8):
+    """mid[s] = bf16(W13[mask[s]] h) for the active slots, NaN rows past the count
+    (numpy_ref.py:256-272). W13 [E, 2I, H] (gate rows then up rows)."""
+    n_active = int(mask[-1])
+    mid = np.full((n_slots, np.shape(W13)[1]), np.nan, F32)
+    for s in range(n_active):
+        mid[s] = linear(h, W13[int(mask[s])])
+    return mid
+
+
+def swiglu_act(mid_row, i):
+    """act = bf16(silu(gate) * up) element by element (numpy_ref.py:288-290)."""
+    mid_row = np.asarray(mid_row, F32)
+    return bf16((silu(mid_row[:i]) * mid_row[i:2 * i]).astype(F32))
+
+
+def moe_w2(mid, W2, mask, n_slots=8):
+    """out8[s] = bf16(W2[e] act_s), act_s = bf16(silu(gate) * up) (numpy_ref.py:275-292)."""
+    k = np.shape(W2)[2]
+    n_active = int(mask[-1])
+    out = np.full((n_slots, np.shape(W2)[1]), np.nan, F32)
+    for s in range(n_active):
+        out[s] = linear(swiglu_act(mid[s], k), W2[int(mask[s])])
+    return out
+
+
+def moe_combine(out8, topk_w, x_res):
+    """x + sum_k w_k out_k in slot order, then one BF16 rounding (numpy_ref.py:316-321, the stock
+    moe_mul_sum_add). Each product (FP32 weight x BF16 value) is exact in FP64 and the FP64 sums
+    run in slot order, so the kernel's identical sequence gives identical bits."""
+    acc = np.asarray(x_res, F64).copy()
+    for k in range(len(topk_w)):
+        acc = acc + np.asarray(out8[k], F64) * F64(F32(topk_w[k]))
+    return bf16_from_f64(acc)
+
+
+def dense_mlp(h, W_gu, W_down, x_res, i_dense):
+    """Layer 0's SwiGLU MLP (stock gang_linear_silu + linear_with_residual, plan
+    fleet/graph_plan.py:507-526), with the expert arithmetic: mid = bf16(W_gu h) [gate; up],
+    act = bf16(silu(gate) * up), x_res = bf16(W_down act + x_res). Returns (mid, act, x_res)."""
+    mid = linear(h, W_gu)
+    act = swiglu_act(mid, i_dense)
+    return mid, act, linear_residual(act, W_down, x_res)
+
+
+# ---------------------------------------------------------------------------------------------
+# prologue and head
+
+
+def embed(W_embed, token):
+    """x_res = W_embed[token] (the stock embedding task, fleet/graph_plan.py:416-418)."""
+    return np.asarray(W_embed[int(token)], F32).copy()
+
+
+def lm_head_argmax(x_res, w_final_norm, W_lm, eps=1e-6):
+    """h = rmsnorm(x_res); logits = bf16(W_lm h); token = argmax, lowest index on ties
+    (fleet/graph_plan.py:570-602; torch.argmax as harness/run_reference.py:395 uses it).
+    Returns (h, logits, token)."""
+    h = rmsnorm(x_res, w_final_norm, eps)
+    logits = linear(h, W_lm)
+    return h, logits, int(np.argmax(logits))

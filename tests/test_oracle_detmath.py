@@ -1,0 +1,115 @@
+"""The oracle's deterministic arithmetic: BF16 rounding against torch, the straight FP64->BF16
+rounding against exact rational rounding, and det_exp / det_log against FP64 error bounds."""
+import math
+from fractions import Fraction
+
+import numpy as np
+import torch
+
+from oracle import detmath as D
+
+
+def ulp_err(got, exact):
+    """|got - exact| in FP32 ulps of the exact value (FP64 exact)."""
+    exact = np.asarray(exact, np.float64)
+    got = np.asarray(got, np.float64)
+    e = np.floor(np.log2(np.maximum(np.abs(exact), 2.0 ** -126)))
+    ulp = 2.0 ** (e - 23)
+    return np.abs(got - exact) / ulp
+
+
+def test_bf16_matches_torch():
+    xs = np.random.default_rng(0).standard_normal(100000).astype(np.float32) * 100
+    xs = np.concatenate([xs, np.array([1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5e-3, 65504.0, 0.0, -0.0], np.float32)])
+    assert np.array_equal(D.bf16(xs), torch.tensor(xs).bfloat16().float().numpy())
+
+
+def _bf16_exact_round(v):
+    """Round a Fraction to the nearest BF16 (ties to even), normal range."""
+    if v == 0:
+        return 0.0
+    s = -1 if v < 0 else 1
+    a = abs(v)
+    e = math.floor(math.log2(a))
+    while Fraction(2) ** e > a:
+        e -= 1
+    while Fraction(2) ** (e + 1) <= a:
+        e += 1
+    q = a / Fraction(2) ** (e - 7)               # 8 significant bits
+    n = math.floor(q)
+    r = q - n
+    if r > Fraction(1, 2) or (r == Fraction(1, 2) and n % 2 == 1):
+        n += 1
+    return s * float(n * Fraction(2) ** (e - 7))
+
+
+def test_bf16_from_f64_is_one_rounding():
+    rng = np.random.default_rng(1)
+    xs = rng.standard_normal(3000) * np.exp(rng.uniform(-20, 20, 3000))
+    # values that a double rounding through FP32 would get wrong: just above a BF16 midpoint
+    mids = np.array([1.0 + 2 ** -8 + 2 ** -40, 1.0 + 2 ** -8 - 2 ** -40, -(3.0 + 2 ** -7 + 2 ** -35)])
+    xs = np.concatenate([xs, mids])
+    got = D.bf16_from_f64(xs)
+    want = np.array([_bf16_exact_round(Fraction(float(x))) for x in xs], np.float32)
+    assert np.array_equal(got, want)
+    # an FP32 detour would round 1 + 2^-8 + 2^-40 to the midpoint and then to even (1.0)
+    assert D.bf16_from_f64(np.array([1.0 + 2 ** -8 + 2 ** -40]))[0] == np.float32(1.0 + 2 ** -7)
+
+
+def test_bf16_from_f64_subnormal_and_specials():
+    xs = np.array([2.0 ** -130, -3 * 2.0 ** -134, np.inf, -np.inf, 3.5e38, np.nan])
+    got = D.bf16_from_f64(xs)
+    assert got[0] == np.float32(2.0 ** -130)
+    assert got[1] == np.float32(-2.0 ** -132)        # 1.5 ulp of the 2^-133 grid -> 2 (even)
+    assert got[2] == np.inf and got[3] == -np.inf and got[4] == np.inf and np.isnan(got[5])
+
+
+def test_det_exp_error_bound():
+    rng = np.random.default_rng(2)
+    xs = np.concatenate([rng.uniform(-87, 88, 200000), rng.uniform(-1, 1, 50000),
+                         np.array([0.0, -0.0, 1e-30, -1e-30, 88.0, -87.0])]).astype(np.float32)
+    got = D.det_exp(xs)
+    exact = np.exp(xs.astype(np.float64))
+    assert got.dtype == np.float32
+    normal = exact >= 2.0 ** -126
+    assert ulp_err(got[normal], exact[normal]).max() < 2.0
+    assert D.det_exp(np.float32(0.0)) == 1.0
+    sp = D.det_exp(np.array([-np.inf, -100.0, 100.0, np.inf, np.nan], np.float32))
+    assert sp[0] == 0 and sp[1] == 0 and sp[2] == np.inf and sp[3] == np.inf and np.isnan(sp[4])
+
+
+def test_det_log_error_bound():
+    rng = np.random.default_rng(3)
+    xs = np.concatenate([np.exp(rng.uniform(-80, 80, 200000)), rng.uniform(0.5, 2.0, 50000),
+                         rng.uniform(1.0, 64.0, 50000), np.array([1.0, 2.0, 1e-40, 3e-45])]).astype(np.float32)
+    xs = xs[xs > 0]
+    got = D.det_log(xs)
+    exact = np.log(xs.astype(np.float64))
+    err = np.abs(got.astype(np.float64) - exact)
+    ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(exact), 2.0 ** -126))) - 23)
+    # worst near x = 1 (e = 0), where the rounding of m + 1 and of the quotient dominate
+    assert (err / ulp).max() < 3.0
+    assert D.det_log(np.float32(1.0)) == 0.0
+    sp = D.det_log(np.array([0.0, -1.0, np.inf, np.nan], np.float32))
+    assert sp[0] == -np.inf and np.isnan(sp[1]) and sp[2] == np.inf and np.isnan(sp[3])
+
+
+def test_silu_close_to_exact():
+    xs = np.random.default_rng(4).uniform(-30, 30, 100000).astype(np.float32)
+    got = D.silu(xs).astype(np.float64)
+    x64 = xs.astype(np.float64)
+    exact = x64 / (1.0 + np.exp(-x64))
+    assert np.all(np.abs(got - exact) <= 4 * np.abs(exact) * 2.0 ** -24 + 1e-37)
+
+
+def test_dot_exact_order_free():
+    """The FP64 sum of exact BF16 products rounds the same in any order (what lets a GPU
+    reduction tree and NumPy agree bit for bit)."""
+    rng = np.random.default_rng(5)
+    W = D.bf16(rng.standard_normal((64, 2048)).astype(np.float32) * 0.02)
+    x = D.bf16(rng.standard_normal(2048).astype(np.float32))
+    a = D.bf16_from_f64(D.dot_exact(W, x))
+    perm = rng.permutation(2048)
+    b = D.bf16_from_f64(D.dot_exact(W[:, perm], x[perm]))
+    c = D.bf16_from_f64(np.array([sum(float(W[i, k]) * float(x[k]) for k in range(2048)) for i in range(64)]))
+    assert np.array_equal(a, b) and np.array_equal(a, c)

@@ -1,0 +1,207 @@
+"""Pin the CPU oracle to the reference.
+
+1. Against the reference's NumPy specification (harness/numpy_ref.py), run on the same seeded
+   inputs by tests/golden/make_golden.py: identical where the reference's arithmetic is
+   order-free (BF16 rounding, RoPE, router ids/mask/routing, the tie rule), and within the
+   reference's own kernel tolerances (fleet/tasks/kernel_tests.py:120-171) where the reference
+   sums in an unspecified FP32 order and the oracle sums exactly.
+2. Against the reference model's own modules (modeling_deepseek.py, tiny random model):
+   the oracle composed into the decode step, fed the model's weights and its prefill latent
+   cache, reproduces the model's greedy ids and routed experts over 6 steps, and its per-layer
+   boundaries within the reference's boundary classes (harness/common.py:28-40).
+"""
+import json
+
+import numpy as np
+import pytest
+
+from oracle import numpy_ref as R
+from oracle.detmath import from_bf16_bits
+from oracle.model import OracleModel
+
+F32_REL = 1e-4        # kernel_tests.py:165
+BF16_REL = 2e-3       # kernel_tests.py:166
+BF16_ULP = 2.0 ** -7  # kernel_tests.py:167
+PARTIALS_O_REL = 5e-4
+LSE_ABS = 1e-4
+
+
+def rel(a, b):
+    a, b = np.asarray(a, np.float64).reshape(-1), np.asarray(b, np.float64).reshape(-1)
+    return np.linalg.norm(a - b) / np.linalg.norm(b)
+
+
+def bf16_close(got, ref):
+    """The reference's per-element BF16 bound (kernel_tests.py:134-145) and rel_err <= 2e-3."""
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    bound = BF16_ULP * np.abs(ref) + 1e-5 * np.abs(ref).max()
+    return bool(np.all(np.abs(got - ref) <= bound)) and rel(got, ref) <= BF16_REL
+
+
+@pytest.fixture(scope="module")
+def nr(golden):
+    return golden("numpy_ref_cases.npz")
+
+
+def test_bf16_identical(nr):
+    assert np.array_equal(R.bf16(nr["bf16_in"]), nr["bf16_out"])
+
+
+def test_rmsnorm(nr):
+    got = np.stack([R.rmsnorm(x, nr["rms_w"]) for x in nr["rms_x"]])
+    assert bf16_close(got, nr["rms_out"])
+    # the exact sum of squares moves the BF16 result of at most a handful of elements
+    assert (got != nr["rms_out"]).mean() < 0.01
+
+
+def test_rope_identical(nr):
+    assert np.array_equal(R.rope(nr["rope_x"], nr["rope_cos"], nr["rope_sin"]), nr["rope_out"])
+
+
+def test_mla_prep(nr):
+    nh, d_n, d_r, d_c, s_max, step, split = nr["mla_dims"]
+    c_row, k_row, ql, q_pe = R.mla_prep(nr["mla_qkva"], nr["mla_w_kv"], nr["mla_W_uk"], nr["mla_cos"],
+                                        nr["mla_sin"], nh=nh, d_n=d_n, d_r=d_r, d_c=d_c)
+    assert np.array_equal(k_row, nr["mla_k_row"]) and np.array_equal(q_pe, nr["mla_q_pe"])
+    assert bf16_close(c_row, nr["mla_c_row"])
+    assert bf16_close(ql, nr["mla_ql_nope"])
+
+
+def test_mla_attend_and_merge(nr):
+    nh, d_n, d_r, d_c, s_max, step, split = (int(v) for v in nr["mla_dims"])
+    p, s = R.mla_attend(nr["mla_ql_nope"], nr["mla_q_pe"], nr["mla_c_kv"], nr["mla_k_pe"], step,
+                        float(nr["mla_scale"]), split=split, debug_scores=True)
+    ref = nr["mla_partials"]
+    assert p.shape == ref.shape
+    assert rel(s, nr["mla_scores"]) < F32_REL
+    live = -(-(step + 1) // split)
+    assert rel(p[:live, :, :d_c], ref[:live, :, :d_c]) < PARTIALS_O_REL
+    assert np.abs(p[:live, :, d_c] - ref[:live, :, d_c]).max() < LSE_ABS
+    assert np.isneginf(p[live:, :, d_c]).all() and not p[live:, :, :d_c].any()   # empty splits
+    assert rel(R.merge_partials(p, step, split=split), nr["mla_merged"]) < PARTIALS_O_REL
+    assert bf16_close(R.mla_merge_uv(p, nr["mla_W_uv"], step, split=split), nr["mla_attn"])
+
+
+def test_router_ids_identical(nr):
+    logits, w, routing, mask = R.moe_router(nr["router_h"], nr["router_W"], topk=4, n_experts=16, forced=(16, 17))
+    assert rel(logits, nr["router_logits"]) < F32_REL
+    assert np.array_equal(mask, nr["router_mask"]) and np.array_equal(routing, nr["router_routing"])
+    assert rel(w, nr["router_topk_w"]) < F32_REL
+
+
+def test_router_tie_to_lower_index(nr):
+    """Two experts with bit-identical logits: both implementations take the lower id first."""
+    logits, w, routing, mask = R.moe_router(nr["router_h"], nr["tie_W"], topk=4, n_experts=16, forced=(16, 17))
+    lo, hi = (int(v) for v in nr["tie_pair"])
+    assert np.array_equal(mask, nr["tie_mask"])
+    assert list(mask[:2]) == [lo, hi]
+
+
+def test_router_norm(nr):
+    h, logits, w, routing, mask = R.moe_router_norm(nr["rnorm_x"], nr["rnorm_w"], nr["router_W"], topk=4,
+                                                    n_experts=16, forced=(16, 17))
+    assert bf16_close(h, nr["rnorm_h"])
+    assert np.array_equal(mask, nr["rnorm_mask"])
+    assert rel(w, nr["rnorm_topk_w"]) < F32_REL
+
+
+def test_experts_and_combine(nr):
+    mid = R.moe_w13(nr["router_h"], nr["exp_W13"], nr["exp_mask"], n_slots=6)
+    assert bf16_close(mid, nr["exp_mid"])
+    out8 = R.moe_w2(nr["exp_mid"], nr["exp_W2"], nr["exp_mask"], n_slots=6)
+    assert bf16_close(out8, nr["exp_out8"])
+    comb = R.moe_combine(nr["exp_out8"], nr["exp_w"], nr["exp_xres"])
+    assert bf16_close(comb, nr["exp_combined"])
+
+
+def test_linears(nr):
+    assert bf16_close(R.linear(nr["lin_x"], nr["lin_W"]), nr["lin_out"])
+    assert bf16_close(R.linear_residual(nr["lin_x"], nr["lin_W"], nr["lin_res"]), nr["lin_res_out"])
+
+
+# ---------------------------------------------------------------------------------------------
+# the reference model's modules
+
+
+class TinyDims:
+    def __init__(self, c):
+        self.H, self.NH, self.D_N, self.D_R = c["hidden_size"], c["num_attention_heads"], c["qk_nope_head_dim"], c["qk_rope_head_dim"]
+        self.D_V, self.D_C, self.V, self.L = c["v_head_dim"], c["kv_lora_rank"], c["vocab_size"], c["num_hidden_layers"]
+        self.I_DENSE, self.I_MOE, self.E = c["intermediate_size"], c["moe_intermediate_size"], c["n_routed_experts"]
+        self.TOPK, self.N_SHARED = c["num_experts_per_tok"], c["n_shared_experts"]
+        self.E_TOTAL, self.N_SLOTS = self.E + self.N_SHARED, self.TOPK + self.N_SHARED
+        self.QKVA_OUT = self.NH * (self.D_N + self.D_R) + self.D_C + self.D_R
+
+
+@pytest.fixture(scope="module")
+def tiny(golden):
+    import torch
+    from fleet.pack_weights import Dims, pack_state_dict
+
+    fx = golden("hf_tiny.npz")
+    cfg = json.loads(str(fx["config"]))
+    sd = {k[2:]: torch.from_numpy(fx[k].astype(np.int16)).view(torch.bfloat16) for k in fx.files if k.startswith("w:")}
+    dims = Dims.from_config(cfg)
+    packed = {k: v.float().numpy() for k, v in pack_state_dict(dims, sd).items()}
+    return fx, cfg, dims, packed
+
+
+def test_tiny_model_greedy_ids_and_routes(tiny):
+    """The oracle decodes the reference model's own greedy ids and routed experts."""
+    fx, cfg, dims, packed = tiny
+    prefill = int(fx["prefill"])
+    steps = len(fx["ids"])
+    s_max = prefill + steps + 1
+    cos, sin = from_bf16_bits(fx["cos"]), from_bf16_bits(fx["sin"])
+    cache = {}
+    for l in range(dims.L):
+        cache[f"c_kv_{l}"] = fx["cache_c"][l].copy()
+        cache[f"k_pe_{l}"] = fx["cache_k"][l].copy()
+    tokens = np.zeros(s_max + 1, np.int64)
+    tokens[:prefill + 1] = fx["prompt"]
+    m = OracleModel(dims, packed.__getitem__, softmax_scale=float(fx["softmax_scale"]), split=4,
+                    eps=cfg["rms_norm_eps"])
+    ids, routes, _ = m.generate(tokens, prefill, steps, cache, cos, sin)
+    assert ids == fx["ids"].tolist()
+    ref_routes = fx["routes"].tolist()
+    for s in range(steps):
+        for j in range(dims.L - 1):
+            assert sorted(routes[s][j]) == sorted(ref_routes[s][j]), (s, j)
+
+
+def test_tiny_model_step0_boundaries(tiny):
+    """Step 0 of the decode: per-layer boundaries within the reference's class thresholds
+    (harness/common.py:28-40): norm 1e-2, gemv 2e-2, attention 3e-2, expert 3e-2, layer 5e-2,
+    logits 5e-2; the cache row's RoPE half bit-exact."""
+    fx, cfg, dims, packed = tiny
+    prefill = int(fx["prefill"])
+    s_max = prefill + len(fx["ids"]) + 1
+    cos, sin = from_bf16_bits(fx["cos"]), from_bf16_bits(fx["sin"])
+    cache = {}
+    for l in range(dims.L):
+        cache[f"c_kv_{l}"] = fx["cache_c"][l].copy()
+        cache[f"k_pe_{l}"] = fx["cache_k"][l].copy()
+    m = OracleModel(dims, packed.__getitem__, softmax_scale=float(fx["softmax_scale"]), split=4,
+                    eps=cfg["rms_norm_eps"])
+    tok, _, rec = m.step(int(fx["prompt"][prefill]), prefill, cache, cos, sin, record=True)
+    for l in range(dims.L):
+        assert rel(rec[f"L{l}.norm1"], fx[f"b_L{l}_norm1"]) < 1e-2
+        q_out = dims.NH * (dims.D_N + dims.D_R)
+        assert rel(rec[f"L{l}.qkva"][:q_out], fx[f"b_L{l}_q"]) < 2e-2
+        assert rel(rec[f"L{l}.qkva"][q_out:], fx[f"b_L{l}_kva"]) < 2e-2
+        assert rel(rec[f"L{l}.c_kv"], fx[f"b_L{l}_c_row"]) < 1e-2
+        assert rel(rec[f"L{l}.k_pe"], fx[f"b_L{l}_k_row"]) < 1e-2
+        assert rel(rec[f"L{l}.attn"], fx[f"b_L{l}_attn"]) < 3e-2
+        assert rel(rec[f"L{l}.x_res_attn"], fx[f"b_L{l}_x_res_attn"]) < 2e-2
+        assert rel(rec[f"L{l}.norm2"], fx[f"b_L{l}_norm2"]) < 1e-2
+        assert rel(rec[f"L{l}.layer_out"], fx[f"b_L{l}_layer_out"]) < 5e-2
+        if l > 0:
+            mask = rec[f"L{l}.mask"]
+            for s in range(dims.TOPK):
+                assert rel(rec[f"L{l}.out8"][s], fx[f"b_L{l}_experts"][s]) < 3e-2
+            shared = rec[f"L{l}.out8"][dims.TOPK:dims.N_SLOTS].astype(np.float64).sum(0)
+            assert rel(shared, fx[f"b_L{l}_shared"]) < 3e-2
+            assert list(mask[:dims.TOPK]) == fx["routes"][0][l - 1].tolist()
+    assert rel(rec["head.norm"], fx["b_head_norm"]) < 1e-2
+    assert rel(rec["head.logits"], fx["b_head_logits"]) < 5e-2
+    assert tok == int(fx["ids"][0])
