@@ -1,0 +1,227 @@
+// mk_ops.cuh -- the task kernels of the decode graph, as device functions of the persistent
+// kernel. Each operator type has a producer half (which global bytes its tasks stream through
+// the shared-memory ring, issued by the producer warp) and a consumer half (what the eight
+// consumer warps compute from those stages and from activations in L2).
+//
+// Arithmetic contract (oracle/numpy_ref.py is the CPU statement of it): every dot product of
+// BF16 values accumulates exact products in FP64 (any order) and is rounded once; every exp/log
+// is det_exp/det_log; the rounding points are the reference's (harness/numpy_ref.py:36-321).
+#pragma once
+#include "mk_device.cuh"
+
+namespace mk {
+
+// ---- per-launch iteration context ----------------------------------------------------------
+
+struct Iter {
+  int32_t it;       // iteration within this launch
+  int32_t pos;      // decode position (cache row written, token read)
+  uint32_t g;       // global generation (1-based)
+};
+
+struct Cons {       // consumer-side state
+  uint32_t c_it, c_rel;
+  int warp, lane, tid;
+};
+
+// ---- error reporting ------------------------------------------------------------------------
+
+__device__ __noinline__ void report_error(const KernelParams& P, Smem& sm, uint32_t code, uint32_t op,
+                                          uint32_t task, uint32_t info) {
+  if (atomicCAS(&P.status->error, 0u, code) == 0u) {
+    P.status->err_op = op;
+    P.status->err_task = task;
+    P.status->err_cta = blockIdx.x;
+    P.status->err_info = info;
+    __threadfence();
+  }
+  atomicExch(&P.status->abort_flag, 1u);
+  *(volatile uint32_t*)&sm.cta_abort = 1u;
+}
+
+__device__ __forceinline__ bool aborted(const KernelParams& P, Smem& sm) {
+  return *(volatile uint32_t*)&sm.cta_abort || *(volatile uint32_t*)&P.status->abort_flag;
+}
+
+// Bounded spin until *ev >= target (wrap-safe). `never` models the debug hook (an event that
+// never fires). Returns false on timeout or when another CTA has aborted.
+__device__ __noinline__ bool wait_event(const KernelParams& P, Smem& sm, const uint32_t* ev, uint32_t target,
+                                        bool never) {
+  if (!never && (int32_t)(ld_acquire_u32(ev) - target) >= 0) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t n = 1;; ++n) {
+    if (!never && (int32_t)(ld_acquire_u32(ev) - target) >= 0) return true;
+    if ((n & 31u) == 0u) {
+      if (aborted(P, sm)) return false;
+      if ((int64_t)(globaltimer() - t0) > P.timeout_ns) return false;
+    }
+  }
+}
+
+// Bounded wait on a ring mbarrier phase.
+__device__ __noinline__ bool ring_wait(const KernelParams& P, Smem& sm, uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((n & 7u) == 0u) {
+      if (aborted(P, sm)) return false;
+      if ((int64_t)(globaltimer() - t0) > P.timeout_ns) return false;
+    }
+  }
+}
+
+// ---- consumer ring access -------------------------------------------------------------------
+
+__device__ __forceinline__ uint8_t* acquire_stage(const KernelParams& P, Smem& sm, Cons& c, uint32_t op,
+                                                  uint32_t task) {
+  const uint32_t st = c.c_it % NSTAGES, ph = (c.c_it / NSTAGES) & 1u;
+  if (!*(volatile uint32_t*)&sm.cta_abort && !ring_wait(P, sm, &sm.full[st], ph)) {
+    if (c.lane == 0)
+      report_error(P, sm, *(volatile uint32_t*)&P.status->abort_flag ? MK_DERR_ABORTED : MK_DERR_RING_TIMEOUT,
+                   op, task, 1);
+  }
+  c.c_it++;
+  return sm.ring[st];
+}
+__device__ __forceinline__ uint8_t* stage_ptr(Smem& sm, uint32_t index) { return sm.ring[index % NSTAGES]; }
+__device__ __forceinline__ void release_stage(Smem& sm, Cons& c) {
+  const uint32_t st = c.c_rel % NSTAGES;
+  c.c_rel++;
+  __syncwarp();
+  if (c.lane == 0) mbar_arrive(&sm.empty[st]);
+}
+
+// ---- FP64 exact dot products ----------------------------------------------------------------
+
+// x' (activation scaled by 2^832) for vectors v = lane + 32 j of a K-slice; x is BF16 bits.
+template <int MAXV, bool SMEM>
+__device__ __forceinline__ void load_x(double (&xr)[MAXV][8], const uint16_t* x, int klen, int lane) {
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int v = lane + 32 * j;
+    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+    if (v * 8 < klen) raw = SMEM ? *reinterpret_cast<const uint4*>(x + v * 8) : ldcg16(x + v * 8);
+    xr[j][0] = xprime(bf16_bits_to_f32(raw.x & 0xFFFFu));
+    xr[j][1] = xprime(bf16_bits_to_f32(raw.x >> 16));
+    xr[j][2] = xprime(bf16_bits_to_f32(raw.y & 0xFFFFu));
+    xr[j][3] = xprime(bf16_bits_to_f32(raw.y >> 16));
+    xr[j][4] = xprime(bf16_bits_to_f32(raw.z & 0xFFFFu));
+    xr[j][5] = xprime(bf16_bits_to_f32(raw.z >> 16));
+    xr[j][6] = xprime(bf16_bits_to_f32(raw.w & 0xFFFFu));
+    xr[j][7] = xprime(bf16_bits_to_f32(raw.w >> 16));
+  }
+}
+
+// One BF16 row (in shared memory) against x'; the warp-reduced exact dot product (all lanes).
+template <int MAXV>
+__device__ __forceinline__ double row_dot(const double (&xr)[MAXV][8], const uint8_t* row, int klen, int lane) {
+  double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int v = lane + 32 * j;
+    if (v * 8 < klen) {
+      const uint4 w = *reinterpret_cast<const uint4*>(row + v * 16);
+      a0 = fma(wlo_f64(w.x), xr[j][0], a0);
+      a1 = fma(whi_f64(w.x), xr[j][1], a1);
+      a2 = fma(wlo_f64(w.y), xr[j][2], a2);
+      a3 = fma(whi_f64(w.y), xr[j][3], a3);
+      a0 = fma(wlo_f64(w.z), xr[j][4], a0);
+      a1 = fma(whi_f64(w.z), xr[j][5], a1);
+      a2 = fma(wlo_f64(w.w), xr[j][6], a2);
+      a3 = fma(whi_f64(w.w), xr[j][7], a3);
+    }
+  }
+  double a = (a0 + a1) + (a2 + a3);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+  return a * DOT_UNSCALE;
+}
+
+__device__ __forceinline__ double warp_sum_f64(double a) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+  return a;
+}
+__device__ __forceinline__ float warp_max_f32(float a) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  return a;
+}
+
+// ---- RMSNorm of a BF16 row into shared memory (all 256 consumer threads) ----------------------
+// h = bf16(w * bf16(x * r)), r = 1 / sqrt(f32(exact sum x^2 / K) + eps)   (numpy_ref.py:54-60)
+__device__ void rmsnorm_to_smem(const uint16_t* x, const uint16_t* w, int K, float eps, uint16_t* hbuf, Smem& sm,
+                                const Cons& c) {
+  double ss = 0.0;
+  for (int i = c.tid; i < K; i += NUM_CONSUMERS) {
+    const double v = (double)bf16_bits_to_f32(ldcg_u16(x + i));
+    ss = fma(v, v, ss);
+  }
+  ss = warp_sum_f64(ss);
+  if (c.lane == 0) sm.red[c.warp] = ss;
+  consumer_sync();
+  double tot = 0.0;
+#pragma unroll
+  for (int k = 0; k < NUM_CONSUMER_WARPS; ++k) tot += sm.red[k];
+  const float var = __double2float_rn(tot / (double)K);
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  for (int i = c.tid; i < K; i += NUM_CONSUMERS) {
+    const float v = bf16_bits_to_f32(ldcg_u16(x + i));
+    const float xn = round_bf16(__fmul_rn(v, r));
+    const float wv = bf16_bits_to_f32(__ldg(w + i));
+    hbuf[i] = (uint16_t)f32_to_bf16_bits(__fmul_rn(wv, xn));
+  }
+  consumer_sync();   // hbuf complete; sm.red free again
+}
+
+// RoPE of one d-vector (de-interleaved pairs; numpy_ref.py:63-71): element i of the output.
+__device__ __forceinline__ uint16_t rope_elem(const uint16_t* x, const uint16_t* cosr, const uint16_t* sinr, int d,
+                                              int i, bool x_global) {
+  const int h = d / 2;
+  auto ld = [&](int k) -> float { return bf16_bits_to_f32(x_global ? ldcg_u16(x + k) : (uint32_t)x[k]); };
+  const float xi = (i < h) ? ld(2 * i) : ld(2 * (i - h) + 1);
+  const float rot = (i < h) ? -ld(2 * i + 1) : ld(2 * (i - h));
+  const float cs = bf16_bits_to_f32(__ldg(cosr + i)), sn = bf16_bits_to_f32(__ldg(sinr + i));
+  const float a = round_bf16(__fmul_rn(xi, cs));
+  const float b = round_bf16(__fmul_rn(rot, sn));
+  return (uint16_t)f32_to_bf16_bits(__fadd_rn(a, b));
+}
+
+// ---- helpers on operator parameters --------------------------------------------------------
+
+template <typename T>
+__device__ __forceinline__ T* P_(const OpDev& od, int i) { return reinterpret_cast<T*>(od.op.ptr[i]); }
+__device__ __forceinline__ int64_t I_(const OpDev& od, int i) { return od.op.ip[i]; }
+
+// GATEUP: the stages of a task walk its pair range in chunks inside one group.
+struct GuChunk { int group, q, np; };
+__device__ __forceinline__ bool gu_next(const OpDev& od, int& p, int b, GuChunk& ch) {
+  if (p >= b) return false;
+  const int I = (int)I_(od, MK_I_GU_I);
+  const int g = p / I, q = p % I;
+  int np = od.rps / 2;
+  np = min(np, I - q);
+  np = min(np, b - p);
+  ch.group = g; ch.q = q; ch.np = np;
+  p += np;
+  return true;
+}
+
+// ATTEND: the split a task covers at this iteration.
+struct AttSplit { int lo, hi, n_str, has_pos; };
+__device__ __forceinline__ AttSplit att_split(const OpDev& od, const TaskDev& t, int pos) {
+  const int S = (int)I_(od, MK_I_ATT_SPLIT);
+  AttSplit a;
+  a.lo = t.b * S;
+  a.hi = min(a.lo + S, pos + 1);
+  a.n_str = max(0, min(a.lo + S, pos) - a.lo);
+  a.has_pos = (pos >= a.lo && pos < a.lo + S) ? 1 : 0;
+  if (a.lo > pos) { a.hi = a.lo; a.n_str = 0; a.has_pos = 0; }
+  return a;
+}
+__device__ __forceinline__ int att_rps(const OpDev& od) {
+  return STAGE_BYTES / (int)((I_(od, MK_I_ATT_DC) + I_(od, MK_I_ATT_DR)) * 2);
+}
+
+}  // namespace mk

@@ -1,0 +1,322 @@
+#!/usr/bin/env python3
+"""Build the B200 persistent decode kernel from a plan (drop-in for the reference's
+fleet/build_graph.py: build(), make_meta(), plan_json(), dry_run(), the layer methods).
+
+    mpk, host, plan = build(packed, capture, meta, dims=..., s_max=..., layers=N, head=True)
+    mpk.compile(output_dir=...)       # builds and uploads the schedule (no code generation)
+    mpk()                              # one launch: every remaining greedy iteration
+
+Each plan call becomes one operator of the C library (include/fleet_mk.h) through ctypes; torch
+only allocates the workspaces and hands their device pointers over. `dry_run` drives the same
+code against a recorder, so the plan's checks run without a GPU.
+"""
+import argparse
+import json
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+from fleet import graph_plan as G  # noqa: E402
+from fleet.pack_weights import Dims, REAL_DIMS  # noqa: E402
+
+TORCH_DTYPES = {"bf16": "bfloat16", "f32": "float32", "i32": "int32", "i64": "int64"}
+
+
+# ----------------------------------------------------------------------------
+# the layer methods: plan call -> MkOp
+
+
+def embed_layer(mk, t, input, weight, output):
+    return mk.make_op(mk.OP_EMBED, 0, {0: weight, 1: input, 2: output}, {0: weight.shape[0], 1: weight.shape[1]})
+
+
+def linear_gemv_layer(mk, t, input, weight, output, w_norm=None, residual=None, h_out=None, tokens_out=None,
+                      norm=False, residual_add=False, argmax=False, eps=G.RMS_EPS):
+    N, K = weight.shape
+    assert input.numel() == K and output.numel() == N, (input.shape, weight.shape, output.shape)
+    flags = (mk.F_NORM if norm else 0) | (mk.F_RESIDUAL if residual_add else 0) | (mk.F_ARGMAX if argmax else 0)
+    g = mk.P["gemv"]
+    return mk.make_op(mk.OP_GEMV, flags, {g["X"]: input, g["WNORM"]: w_norm, g["W"]: weight, g["RES"]: residual,
+                                          g["OUT"]: output, g["HOUT"]: h_out, g["TOKENS"]: tokens_out},
+                      {0: N, 1: K}, {0: eps})
+
+
+def mla_prep_layer(mk, t, qkva, w_kv_norm, w_ukT, cos, sin, c_kv, k_pe, ql_nope, q_pe, eps=G.RMS_EPS):
+    nh, d_c, d_n = w_ukT.shape
+    d_r = k_pe.shape[1]
+    assert qkva.numel() == nh * (d_n + d_r) + d_c + d_r
+    return mk.make_op(mk.OP_MLA_PREP, 0, dict(enumerate([qkva, w_kv_norm, w_ukT, cos, sin, c_kv, k_pe, ql_nope, q_pe])),
+                      {0: nh, 1: d_n, 2: d_r, 3: d_c, 4: c_kv.shape[0]}, {0: eps})
+
+
+def mla_attend_layer(mk, t, ql_nope, q_pe, c_kv, k_pe, partials, softmax_scale, split, n_splits, head_group):
+    nh, d_c = ql_nope.shape
+    assert partials.shape == (n_splits, nh, G.partials_row(d_c)), partials.shape
+    return mk.make_op(mk.OP_MLA_ATTEND, 0, dict(enumerate([ql_nope, q_pe, c_kv, k_pe, partials])),
+                      {0: nh, 1: d_c, 2: k_pe.shape[1], 3: c_kv.shape[0], 4: split, 5: head_group, 6: n_splits,
+                       7: partials.shape[2]}, {0: softmax_scale})
+
+
+def mla_merge_uv_layer(mk, t, partials, w_uv, output, split, n_splits):
+    nh, d_v, d_c = w_uv.shape
+    return mk.make_op(mk.OP_MLA_MERGE_UV, 0, {0: partials, 1: w_uv, 2: output},
+                      {0: nh, 1: d_v, 2: d_c, 3: split, 4: n_splits, 5: partials.shape[2]})
+
+
+def moe_router_layer(mk, t, input, w_norm, w_gate, h, topk_w, routing, mask, logits, route_log, layer_index, topk,
+                     n_experts, n_forced, scaling, eps, bias=None):
+    E, H = w_gate.shape
+    r = mk.P["rt"]
+    log_rows, log_layers, log_slots = route_log.shape if route_log is not None else (1, 1, topk + n_forced)
+    return mk.make_op(mk.OP_ROUTER, 0, {r["X"]: input, r["WNORM"]: w_norm, r["WGATE"]: w_gate, r["HOUT"]: h,
+                                        r["LOGITS"]: logits, r["TOPKW"]: topk_w, r["ROUTING"]: routing,
+                                        r["MASK"]: mask, r["ROUTELOG"]: route_log, r["BIAS"]: bias},
+                      {0: H, 1: E, 2: topk, 3: n_forced, 4: layer_index, 5: log_layers * log_slots, 6: log_rows},
+                      {0: eps, 1: scaling})
+
+
+def gateup_layer(mk, t, input, weight, act, inter, groups, expert, norm, w_norm=None, mask=None, mid=None, h_out=None,
+                 eps=G.RMS_EPS):
+    K = weight.shape[-1]
+    estride = weight.shape[-2] * K if weight.dim() == 3 else 0
+    nexp = weight.shape[0] if weight.dim() == 3 else 1
+    flags = (mk.F_EXPERT if expert else 0) | (mk.F_NORM if norm else 0)
+    u = mk.P["gu"]
+    return mk.make_op(mk.OP_GATEUP, flags, {u["X"]: input, u["WNORM"]: w_norm, u["W"]: weight, u["MASK"]: mask,
+                                            u["MID"]: mid, u["ACT"]: act, u["HOUT"]: h_out},
+                      {0: K, 1: inter, 2: groups, 3: estride, 4: nexp}, {0: eps})
+
+
+def moe_w2_combine_layer(mk, t, input, weight, mask, topk_w, residual, output, out8=None):
+    E, H, I = weight.shape
+    assert residual.data_ptr() == output.data_ptr(), "the combine adds into x_res in place"
+    n_slots = input.shape[0]
+    w = mk.P["w2"]
+    return mk.make_op(mk.OP_W2_COMBINE, 0, {w["ACT"]: input, w["W"]: weight, w["MASK"]: mask, w["TOPKW"]: topk_w,
+                                            w["XRES"]: output, w["OUT8"]: out8},
+                      {0: H, 1: I, 2: n_slots, 3: H * I, 4: E})
+
+
+def stream_layer(mk, t, weight, dummy, dummy_in=None):
+    return mk.make_op(mk.OP_STREAM, 0, {0: weight, 1: dummy}, {0: weight.shape[0], 1: weight.shape[1]})
+
+
+NEW_LAYERS = {
+    "embed_layer": embed_layer, "linear_gemv_layer": linear_gemv_layer, "mla_prep_layer": mla_prep_layer,
+    "mla_attend_layer": mla_attend_layer, "mla_merge_uv_layer": mla_merge_uv_layer,
+    "moe_router_layer": moe_router_layer, "gateup_layer": gateup_layer,
+    "moe_w2_combine_layer": moe_w2_combine_layer, "stream_layer": stream_layer,
+}
+
+
+# ----------------------------------------------------------------------------
+# driving the plan
+
+
+def new_workspace(torch, t, device="cuda"):
+    """A zeroed workspace for plan tensor t."""
+    return torch.zeros(t.shape, dtype=getattr(torch, TORCH_DTYPES[t.dtype]), device=device)
+
+
+def allocate_workspaces(torch, plan, device="cuda"):
+    return {t.name: new_workspace(torch, t, device) for t in plan.tensors.values() if t.kind != "input"}
+
+
+def make_tensors(plan, packed, capture, meta, torch, workspaces=None, device="cuda"):
+    """name -> torch tensor for every plan tensor: inputs attached (shape-checked), the rest zeroed."""
+    host = {}
+    workspaces = workspaces or {}
+    for t in plan.tensors.values():
+        if t.kind == "input":
+            if t.source.startswith("meta:"):
+                src = meta[t.source[5:]]
+            elif t.source.startswith("capture:"):
+                src = capture[t.source[8:]]
+            else:
+                src = packed[t.source]
+            assert tuple(src.shape) == t.shape, (t.name, tuple(src.shape), t.shape)
+            assert src.is_contiguous(), t.name
+            host[t.name] = src
+        else:
+            buf = workspaces.get(t.name)
+            if buf is None:
+                buf = new_workspace(torch, t, device)
+            assert tuple(buf.shape) == t.shape, (t.name, tuple(buf.shape), t.shape)
+            host[t.name] = buf
+    return host
+
+
+def call_kwargs(c, host):
+    kw = {}
+    for k, v in c.args.items():
+        if isinstance(v, str) and v in host:
+            kw[k] = host[v]
+        else:
+            kw[k] = v
+    return kw
+
+
+def make_meta(torch, s_max, prompt_ids, n_prompt, device="cuda"):
+    """The meta tensors the reference's runtime reads (fleet/build_graph.py:531-547), with its
+    values: step = n_prompt - 2 (the first iteration runs at n_prompt - 1), tokens[:n_prompt] the
+    prompt. Only `step` and `tokens` are read by this kernel; the rest keep the reference's
+    interface for its callers."""
+    tokens = torch.zeros(1, s_max, dtype=torch.int64, device=device)
+    tokens[0, :n_prompt] = torch.as_tensor(list(prompt_ids), dtype=torch.int64)
+    return {
+        "step": torch.full((1,), n_prompt - 2, dtype=torch.int32, device=device),
+        "tokens": tokens,
+        "input_tokens": torch.zeros(1, 1, dtype=torch.int64, device=device),
+        "output_tokens": torch.zeros(1, 1, dtype=torch.int64, device=device),
+        "num_new_tokens": torch.ones(1, dtype=torch.int32, device=device),
+        "prompt_lengths": torch.full((1,), n_prompt, dtype=torch.int32, device=device),
+        "qo_indptr_buffer": torch.tensor([0, 1], dtype=torch.int32, device=device),
+        "paged_kv_indptr_buffer": torch.zeros(2, dtype=torch.int32, device=device),
+        "paged_kv_indices_buffer": torch.zeros(1, dtype=torch.int32, device=device),
+        "paged_kv_last_page_len_buffer": torch.zeros(1, dtype=torch.int32, device=device),
+    }
+
+
+def plan_json(plan):
+    return {"layers": plan.layers, "head": plan.head, "debug": plan.debug, "s_max": plan.s_max,
+            "split": plan.split, "head_group": plan.head_group, "dims": plan.dims.to_dict(),
+            "tensors": {n: {"shape": list(t.shape), "dtype": t.dtype, "kind": t.kind, "source": t.source}
+                        for n, t in plan.tensors.items()},
+            "calls": [{"method": c.method, "label": c.label, "status": c.status, "tasks": c.tasks,
+                       "args": {k: (list(v) if isinstance(v, tuple) else v) for k, v in c.args.items()}}
+                      for c in plan.calls]}
+
+
+class MPK:
+    """The built graph: mk handle + tensors. compile() uploads the schedule; __call__ runs every
+    iteration left until tokens is full (the reference's mpk(), one launch); launch(iters) runs a
+    given number of iterations from the handle's own step counter (one launch)."""
+
+    def __init__(self, plan, host, meta, kernel):
+        self.plan = plan
+        self.host = host
+        self.meta = meta
+        self.kernel = kernel
+        self.compiled = False
+        self.step = None
+
+    def compile(self, output_dir=None, **_):
+        self.kernel.finalize()
+        for c, i in zip(self.plan.calls, range(len(self.plan.calls))):
+            c.tasks = self.kernel.tasks(i)
+        self.compiled = True
+        if output_dir:
+            Path(output_dir).mkdir(parents=True, exist_ok=True)
+            (Path(output_dir) / "plan.json").write_text(json.dumps(plan_json(self.plan)) + "\n")
+
+    def sync_step(self):
+        """Read meta step from the device (once per __call__)."""
+        self.step = int(self.meta["step"].item())
+
+    def launch(self, iters=1, stream=None):
+        assert self.compiled, "compile() first"
+        if self.step is None:
+            self.sync_step()
+        self.kernel.launch(iters, self.step, stream, self.meta["step"])
+        self.step += iters
+
+    def __call__(self, stream=None):
+        self.sync_step()
+        iters = self.plan.s_max - 2 - self.step
+        assert iters >= 1, f"no iteration left (step {self.step}, s_max {self.plan.s_max})"
+        self.launch(iters, stream)
+
+    def status(self, raise_on_error=True):
+        return self.kernel.status(raise_on_error)
+
+
+def build(packed, capture, meta, dims=REAL_DIMS, s_max=1056, layers=27, head=True, debug=False, stop_after=None,
+          split=G.SPLIT, head_group=G.HEAD_GROUP, num_ctas=0, device=None, trace=False, wait_timeout_s=2.0,
+          plan=None, workspaces=None, logit_bias=False):
+    """On the machine: the plan, its tensors, one library operator per call -> (mpk, host, plan).
+    plan: a ready plan (the stream probe) instead of the model's."""
+    import torch
+    from fleet import mk
+
+    if plan is None:
+        plan = G.build_plan(dims, s_max, layers, head, debug, split, head_group, logit_bias=logit_bias)
+    if stop_after:
+        plan.truncate(stop_after)
+    assert not plan.chain_violations(), f"the chain is broken: {plan.chain_violations()}"
+    dev = device if device is not None else torch.cuda.current_device()
+    host = make_tensors(plan, packed, capture, meta, torch, workspaces, device=f"cuda:{dev}")
+    kernel = mk.MegaKernel(device=dev, num_ctas=num_ctas, trace=trace, wait_timeout_s=wait_timeout_s)
+    for c in plan.calls:
+        op = NEW_LAYERS[c.method](mk, None, **call_kwargs(c, host))
+        kernel.add(op)
+    return MPK(plan, host, meta, kernel), host, plan
+
+
+# ----------------------------------------------------------------------------
+# dry run
+
+
+class FakeTensor:
+    def __init__(self, name, shape, dtype):
+        self.name, self.shape, self.dtype = name, tuple(shape), dtype
+
+    def numel(self):
+        n = 1
+        for s in self.shape:
+            n *= s
+        return n
+
+    def dim(self):
+        return len(self.shape)
+
+    def data_ptr(self):
+        return 0x10000 + (hash(self.name) & 0xFFFFFFF) * 256
+
+
+class FakeMk:
+    """Records operators instead of calling the library (the reference's FakeMPK role)."""
+    OP_EMBED, OP_GEMV, OP_MLA_PREP, OP_MLA_ATTEND, OP_MLA_MERGE_UV, OP_ROUTER, OP_GATEUP, OP_W2_COMBINE, OP_STREAM = range(1, 10)
+    F_NORM, F_RESIDUAL, F_ARGMAX, F_EXPERT = 1, 2, 4, 8
+
+    def __init__(self):
+        from fleet.mk import P
+        self.P = P
+        self.ops = []
+
+    def make_op(self, type_, flags=0, ptrs=None, ips=None, fps=None, ntasks=0):
+        rec = {"type": type_, "flags": flags, "ptrs": {k: (v.name if hasattr(v, "name") else v) for k, v in (ptrs or {}).items() if v is not None},
+               "ips": dict(ips or {}), "fps": dict(fps or {})}
+        self.ops.append(rec)
+        return rec
+
+
+def dry_run(dims=REAL_DIMS, s_max=1056, layers=27, head=True, debug=False, stop_after=None, split=G.SPLIT,
+            head_group=G.HEAD_GROUP):
+    """The plan and every operator's parameters, without a GPU: returns (plan, recorded ops)."""
+    plan = G.build_plan(dims, s_max, layers, head, debug, split, head_group)
+    if stop_after:
+        plan.truncate(stop_after)
+    assert not plan.chain_violations(), plan.chain_violations()
+    host = {n: FakeTensor(n, t.shape, t.dtype) for n, t in plan.tensors.items()}
+    fmk = FakeMk()
+    for c in plan.calls:
+        NEW_LAYERS[c.method](fmk, None, **call_kwargs(c, host))
+    return plan, fmk.ops
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--dry-run", action="store_true")
+    ap.add_argument("--layers", type=int, default=27)
+    ap.add_argument("--no-head", action="store_true")
+    ap.add_argument("--s-max", type=int, default=1056)
+    ap.add_argument("--out", default=None)
+    args = ap.parse_args()
+    plan, ops = dry_run(REAL_DIMS, args.s_max, args.layers, not args.no_head)
+    print(json.dumps(G.summary(plan)))
+    if args.out:
+        Path(args.out).write_text(json.dumps(plan_json(plan)) + "\n")
+
+
+if __name__ == "__main__":
+    main()

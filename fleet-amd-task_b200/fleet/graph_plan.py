@@ -1,0 +1,266 @@
+"""The decode task graph as data: the operator chain of one greedy decode token, the tensors it
+attaches or allocates, and the parameters of every operator.
+
+Same entry points and data model as the reference's fleet/graph_plan.py (Tensor, Call, Plan,
+OUTPUT_ARGS, build_plan, the chain rule :189-199, truncate, summary, partials_row), with the
+B200 operator set of include/fleet_mk.h. Per token the chain is
+
+    prologue.embed
+    per layer l:  L{l}.qkva        GEMV, input RMSNorm fused (reference: norm1 + qkva)
+                  L{l}.mla_prep    cache append at the step row, RoPE, ql_nope = q_nope W_uk
+                  L{l}.mla_attend  split-KV partials over (head group, split) tasks
+                  L{l}.mla_merge_uv  merge of the live splits, attn = o W_uv^T
+                  L{l}.o_proj      GEMV + residual into x_res
+      layer 0:    L0.gate_up       post-attention RMSNorm + gate/up GEMV + SwiGLU (dense, I 10,944)
+                  L0.down          GEMV + residual (K 10,944, split over the eight warps)
+      MoE layers: L{l}.router      post-attention RMSNorm + FP32 router + top-k + forced shared experts
+                  L{l}.w13         gate/up GEMV + SwiGLU of the 8 routed slots
+                  L{l}.w2_combine  down GEMV of the 8 slots + the weighted combine into x_res
+    head.lm_head  GEMV with the final RMSNorm, and the greedy argmax into tokens[pos + 1]
+
+against the reference's final stack (fleet/graph_plan.py:416-602 with harness/run_fleet.py:291-298)
+the norm1/norm2/silu/combine/argmax operators are fused into their neighbours: 218 operators per
+token at 27 layers (the reference: 246).
+"""
+import struct
+from dataclasses import dataclass, field
+
+from fleet.pack_weights import Dims, REAL_DIMS
+
+SPLIT = 64             # latent-cache rows per attention split task
+HEAD_GROUP = 2         # query heads per attention task (8 groups x 17 splits = 136 tasks at 1,056 rows)
+ROUTE_LOG_ROWS = 32    # the reference's route_log [32, L - 1, 8] (fleet/graph_plan.py:376)
+RMS_EPS = 1e-6
+SOFTMAX_SCALE = 0.1147213867929261
+ROUTED_SCALING = 1.0
+
+
+def float_bits(x: float) -> int:
+    """A float parameter as its IEEE-754 bit pattern (the reference passes floats this way)."""
+    return struct.unpack("<i", struct.pack("<f", x))[0]
+
+
+def partials_row(d_c):
+    """Innermost width of the split-KV partials: D_C values of o, the lse at column D_C, padded to a
+    multiple of 4 floats so every [split, head] row is 16-byte aligned (513 -> 516 at D_C 512)."""
+    return ((d_c + 1 + 3) // 4) * 4
+
+
+@dataclass
+class Tensor:
+    name: str
+    shape: tuple
+    dtype: str = "bf16"           # bf16 | f32 | i32 | i64
+    kind: str = "new"             # new (allocated, zeroed) | input (attached: weights, capture, meta)
+    source: str = ""              # inputs: "packed key", "capture:<name>" or "meta:<name>"
+
+    @property
+    def num_dims(self):
+        return len(self.shape)
+
+    def dim(self, i):
+        return self.shape[i]
+
+
+@dataclass
+class Call:
+    method: str
+    args: dict
+    tasks: int = 0                # filled by build_graph from the library's partition
+    status: str = "new"
+    note: str = ""
+    label: str = ""
+
+
+# Which argument names of each method are outputs (the rest are inputs). Every operator must read
+# a tensor its predecessor wrote (the reference runtime's chain rule, register_mugraph).
+OUTPUT_ARGS = {
+    "embed_layer": ["output"],
+    "linear_gemv_layer": ["output", "h_out", "tokens_out"],
+    "mla_prep_layer": ["c_kv", "k_pe", "ql_nope", "q_pe"],
+    "mla_attend_layer": ["partials"],
+    "mla_merge_uv_layer": ["output"],
+    "moe_router_layer": ["h", "topk_w", "routing", "mask", "logits", "route_log"],
+    "gateup_layer": ["act", "mid", "h_out"],
+    "moe_w2_combine_layer": ["output", "out8"],
+    "stream_layer": ["dummy"],
+}
+
+
+def _tensor_args(call, names):
+    out = set()
+    for k in names:
+        v = call.args.get(k)
+        if v is None:
+            continue
+        out.update(v if isinstance(v, (tuple, list)) else [v])
+    return out
+
+
+@dataclass
+class Plan:
+    dims: Dims
+    s_max: int
+    layers: int
+    head: bool
+    debug: bool = False
+    split: int = SPLIT
+    head_group: int = HEAD_GROUP
+    tensors: dict = field(default_factory=dict)
+    calls: list = field(default_factory=list)
+
+    def t(self, name, shape, dtype="bf16", kind="new", source=""):
+        assert name not in self.tensors, name
+        self.tensors[name] = Tensor(name, tuple(shape), dtype, kind, source)
+        return name
+
+    def op(self, method, label, note="", **args):
+        self.calls.append(Call(method, args, 0, "new", note, label))
+
+    def index_of(self, label):
+        for i, c in enumerate(self.calls):
+            if c.label == label:
+                return i
+        raise KeyError(label)
+
+    def truncate(self, stop_label):
+        """Keep the calls up to and including the labelled operator (the reference's --stop-after)."""
+        self.calls = self.calls[: self.index_of(stop_label) + 1]
+        return self
+
+    def chain_violations(self):
+        bad = []
+        for prev, cur in zip(self.calls, self.calls[1:]):
+            outs = _tensor_args(prev, OUTPUT_ARGS[prev.method])
+            ins = _tensor_args(cur, [k for k in cur.args if k not in OUTPUT_ARGS[cur.method]])
+            if not (outs & ins):
+                bad.append((prev.label, cur.label))
+        return bad
+
+    @property
+    def n_ops(self):
+        return len(self.calls)
+
+    @property
+    def n_tasks(self):
+        return sum(c.tasks for c in self.calls)
+
+    @property
+    def n_splits(self):
+        return -(-self.s_max // self.split)
+
+
+def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head: bool = True,
+               debug: bool = False, split: int = SPLIT, head_group: int = HEAD_GROUP,
+               route_log_rows: int = ROUTE_LOG_ROWS, logit_bias: bool = False, softmax_scale: float = None) -> Plan:
+    """The operator chain for `layers` layers (+ the head). logit_bias: every router adds an
+    injected FP32 bias [E] to its logits (the skewed/uniform routing of config 3). softmax_scale:
+    default q_head_dim^-0.5 times the YaRN mscale^2 of the dims (0.1147213867929261 at REAL_DIMS)."""
+    from fleet.capture import softmax_scale as yarn_softmax_scale
+    d = dims
+    scale = yarn_softmax_scale(d.D_N, d.D_R) if softmax_scale is None else softmax_scale
+    assert 1 <= layers <= d.L
+    assert d.NH % head_group == 0
+    p = Plan(d, s_max, layers, head, debug, split, head_group)
+    n_splits = p.n_splits
+    # ---- meta, capture and shared activations
+    p.t("tokens", (1, s_max), "i64", "input", "meta:tokens")
+    p.t("W_embed", (d.V, d.H), kind="input", source="W_embed")
+    p.t("cos", (s_max, d.D_R), kind="input", source="capture:cos")
+    p.t("sin", (s_max, d.D_R), kind="input", source="capture:sin")
+    p.t("x_res", (1, d.H))
+    p.t("h", (1, d.H))
+    p.t("qkva", (1, d.QKVA_OUT))
+    p.t("ql_nope", (d.NH, d.D_C))
+    p.t("q_pe", (d.NH, d.D_R))
+    p.t("partials", (n_splits, d.NH, partials_row(d.D_C)), "f32")
+    p.t("attn", (1, d.NH * d.D_V))
+    if layers >= 1:
+        p.t("mid0", (1, 2 * d.I_DENSE))
+        p.t("act0", (1, d.I_DENSE))
+    if layers >= 2:
+        p.t("topk_w", (1, d.N_SLOTS), "f32")
+        p.t("routing", (d.E_TOTAL,), "i32")
+        p.t("mask", (d.E_TOTAL + 1,), "i32")
+        p.t("logits_router", (1, d.E), "f32")
+        p.t("mid", (d.N_SLOTS, 2 * d.I_MOE))
+        p.t("act8", (d.N_SLOTS, d.I_MOE))
+        p.t("out8", (d.N_SLOTS, d.H))
+        p.t("route_log", (route_log_rows, d.L - 1, d.N_SLOTS), "i32")
+    p.op("embed_layer", "prologue.embed", input="tokens", weight="W_embed", output="x_res")
+    for l in range(layers):
+        p.t(f"w_norm1_{l}", (d.H,), kind="input", source=f"w_norm1_{l}")
+        p.t(f"w_norm2_{l}", (d.H,), kind="input", source=f"w_norm2_{l}")
+        p.t(f"W_qkva_{l}", (d.QKVA_OUT, d.H), kind="input", source=f"W_qkva_{l}")
+        p.t(f"w_kv_norm_{l}", (d.D_C,), kind="input", source=f"w_kv_norm_{l}")
+        p.t(f"W_ukT_{l}", (d.NH, d.D_C, d.D_N), kind="input", source=f"W_ukT_{l}")
+        p.t(f"W_uv_{l}", (d.NH, d.D_V, d.D_C), kind="input", source=f"W_uv_{l}")
+        p.t(f"W_o_{l}", (d.H, d.NH * d.D_V), kind="input", source=f"W_o_{l}")
+        p.t(f"c_kv_{l}", (s_max, d.D_C), kind="input", source=f"capture:c_kv_{l}")
+        p.t(f"k_pe_{l}", (s_max, d.D_R), kind="input", source=f"capture:k_pe_{l}")
+        p.op("linear_gemv_layer", f"L{l}.qkva", input="x_res", w_norm=f"w_norm1_{l}", weight=f"W_qkva_{l}",
+             output="qkva", h_out="h", norm=True, eps=RMS_EPS)
+        p.op("mla_prep_layer", f"L{l}.mla_prep", qkva="qkva", w_kv_norm=f"w_kv_norm_{l}", w_ukT=f"W_ukT_{l}",
+             cos="cos", sin="sin", c_kv=f"c_kv_{l}", k_pe=f"k_pe_{l}", ql_nope="ql_nope", q_pe="q_pe", eps=RMS_EPS)
+        p.op("mla_attend_layer", f"L{l}.mla_attend", ql_nope="ql_nope", q_pe="q_pe", c_kv=f"c_kv_{l}",
+             k_pe=f"k_pe_{l}", partials="partials", softmax_scale=scale, split=split, n_splits=n_splits,
+             head_group=head_group)
+        p.op("mla_merge_uv_layer", f"L{l}.mla_merge_uv", partials="partials", w_uv=f"W_uv_{l}", output="attn",
+             split=split, n_splits=n_splits)
+        p.op("linear_gemv_layer", f"L{l}.o_proj", input="attn", weight=f"W_o_{l}", residual="x_res",
+             output="x_res", residual_add=True)
+        if l == 0:
+            p.t("W_gu_0", (2 * d.I_DENSE, d.H), kind="input", source="W_gu_0")
+            p.t("W_down_0", (d.H, d.I_DENSE), kind="input", source="W_down_0")
+            p.op("gateup_layer", "L0.gate_up", input="x_res", w_norm="w_norm2_0", weight="W_gu_0", mid="mid0",
+                 act="act0", h_out="h", groups=1, expert=False, norm=True, eps=RMS_EPS, inter=d.I_DENSE)
+            p.op("linear_gemv_layer", "L0.down", input="act0", weight="W_down_0", residual="x_res", output="x_res",
+                 residual_add=True)
+        else:
+            p.t(f"W_gate_{l}", (d.E, d.H), kind="input", source=f"W_gate_{l}")
+            p.t(f"W13_{l}", (d.E_TOTAL, 2 * d.I_MOE, d.H), kind="input", source=f"W13_{l}")
+            p.t(f"W2_{l}", (d.E_TOTAL, d.H, d.I_MOE), kind="input", source=f"W2_{l}")
+            bias = {}
+            if logit_bias:
+                p.t(f"router_bias_{l}", (d.E,), "f32", kind="input", source=f"capture:router_bias_{l}")
+                bias = dict(bias=f"router_bias_{l}")
+            p.op("moe_router_layer", f"L{l}.router", input="x_res", w_norm=f"w_norm2_{l}", w_gate=f"W_gate_{l}",
+                 h="h", topk_w="topk_w", routing="routing", mask="mask", logits="logits_router",
+                 route_log="route_log", layer_index=l - 1, topk=d.TOPK, n_experts=d.E, n_forced=d.N_SHARED,
+                 scaling=ROUTED_SCALING, eps=RMS_EPS, **bias)
+            p.op("gateup_layer", f"L{l}.w13", input="h", weight=f"W13_{l}", mask="mask", mid="mid", act="act8",
+                 groups=d.N_SLOTS, expert=True, norm=False, inter=d.I_MOE)
+            p.op("moe_w2_combine_layer", f"L{l}.w2_combine", input="act8", weight=f"W2_{l}", mask="mask",
+                 topk_w="topk_w", residual="x_res", output="x_res", out8="out8")
+    if head:
+        p.t("w_final_norm", (d.H,), kind="input", source="w_final_norm")
+        p.t("W_lm", (d.V, d.H), kind="input", source="W_lm")
+        p.t("logits", (1, d.V))
+        p.op("linear_gemv_layer", "head.lm_head", input="x_res", w_norm="w_final_norm", weight="W_lm",
+             output="logits", h_out="h", tokens_out="tokens", norm=True, argmax=True, eps=RMS_EPS)
+    return p
+
+
+def build_stream_plan(ops: int, rows: int, k: int = 2048, dims: Dims = REAL_DIMS) -> Plan:
+    """The bandwidth probe (the reference's stream graph, fleet/graph_plan.py:647-681): `ops`
+    operators, each streaming its own [rows, k] BF16 tensor through the weight ring with no
+    arithmetic, so the ring's read rate is measured with the runtime's scheduling around it."""
+    p = Plan(dims, 1, 0, False)
+    p.t("stream_dummy", (1, 4), "i32")
+    for i in range(ops):
+        p.t(f"stream_w_{i}", (rows, k))
+        p.op("stream_layer", f"S{i}.stream", weight=f"stream_w_{i}", dummy="stream_dummy", dummy_in="stream_dummy")
+    return p
+
+
+def summary(p: Plan) -> dict:
+    ib = 0
+    for t in p.tensors.values():
+        if t.kind == "input":
+            n = 1
+            for s in t.shape:
+                n *= s
+            ib += n * {"bf16": 2, "f32": 4, "i32": 4, "i64": 8}[t.dtype]
+    return {"ops": p.n_ops, "tasks": p.n_tasks, "tensors_new": sum(t.kind == "new" for t in p.tensors.values()),
+            "tensors_input": sum(t.kind == "input" for t in p.tensors.values()), "input_bytes": ib,
+            "n_splits": p.n_splits}

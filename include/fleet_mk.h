@@ -1,0 +1,190 @@
+/*
+ * fleet_mk.h -- C ABI of the B200 (sm_100a) persistent decode megakernel.
+ *
+ * Plain C types only (pointers are device addresses the caller owns; sizes are element
+ * counts); every call returns 0 on success or a negative MK_E* code, with a message from
+ * mk_last_error(). One handle per device; calls on a handle are not re-entrant.
+ *
+ * What these entry points replace in the reference (GolfOscarr/fleet-amd-task, paths within
+ * that project):
+ *   - The runtime's generated C ABI: init_persistent_kernel(std::vector<void*> meta_tensors, ...),
+ *     launch_persistent_kernel(cudaStream_t), finalize_persistent_kernel()
+ *     (hunk headers fleet/patches/new_tasks.patch:301, :374, :384). Here the library is fixed
+ *     (no per-graph code generation): mk_create / mk_add_op / mk_finalize stand for the
+ *     registration plus compile() of fleet/build_graph.py:561-593 and harness/run_fleet.py:556,
+ *     mk_launch for launch_persistent_kernel (mpk(), harness/run_fleet.py:590-592), mk_destroy
+ *     for finalize_persistent_kernel.
+ *   - The per-operator registration _new_task(mpk, grid, block, tensors, task_type, params)
+ *     (fleet/build_graph.py:36-46) and the *_layer methods (fleet/build_graph.py:49-408): one
+ *     mk_add_op per operator, its tensors in MkOp.ptr and its integer parameters in MkOp.ip.
+ *   - The task kernels' contract (fleet/tasks/README.md "Worker contract";
+ *     fleet/tasks/mi300/*.cuh *_task_impl): each MK_OP_* below names the reference task(s)
+ *     whose arithmetic it carries.
+ */
+#ifndef FLEET_MK_H
+#define FLEET_MK_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define MK_ABI_VERSION 1
+
+/* error codes */
+#define MK_OK 0
+#define MK_EINVAL (-1)     /* bad argument or plan */
+#define MK_ECUDA (-2)      /* a CUDA runtime call failed */
+#define MK_ESTATE (-3)     /* call out of order (e.g. add after finalize) */
+#define MK_EDEVICE (-4)    /* the kernel reported an error in its status word */
+
+/* device status error codes (MkStatus.error) */
+#define MK_DERR_NONE 0
+#define MK_DERR_WAIT_TIMEOUT 1     /* an event wait ran past MkConfig.wait_timeout_ns */
+#define MK_DERR_RING_TIMEOUT 2     /* a weight-stream stage did not arrive / free in time */
+#define MK_DERR_TOKEN_RANGE 3      /* a token id outside [0, V) was read (clamped) */
+#define MK_DERR_ABORTED 4          /* another CTA reported an error first */
+#define MK_DERR_BAD_EXPERT 5       /* a routed expert id outside [0, E_TOTAL) */
+
+/* operator types */
+enum MkOpType {
+  MK_OP_EMBED = 1,        /* x_res = W_embed[tokens[pos]]                (stock embedding task) */
+  MK_OP_GEMV = 2,         /* out = bf16(W (norm?(x)) (+ res)), optional fused argmax
+                             (linear_gemv_mi300.cuh:143-252; lm_head + argmax_partial/reduce) */
+  MK_OP_MLA_PREP = 3,     /* cache append, RoPE, ql_nope = q_nope W_uk   (mla_prep_mi300.cuh:34-139) */
+  MK_OP_MLA_ATTEND = 4,   /* split-KV attention partials                 (mla_attend_mi300.cuh:48-280) */
+  MK_OP_MLA_MERGE_UV = 5, /* merge of the splits, attn = o W_uv^T        (mla_merge_uv_mi300.cuh:101-344) */
+  MK_OP_ROUTER = 6,       /* norm2, FP32 logits, softmax, top-k, forced  (moe_router_mi300.cuh:115-354) */
+  MK_OP_GATEUP = 7,       /* mid = W13 h, act = bf16(silu(g) u) per slot (gang_moe_w13_gemv_mi300.cuh;
+                             layer 0's gang_linear_silu) */
+  MK_OP_W2_COMBINE = 8,   /* out8 = W2 act per slot, x += sum w out8     (gang_moe_w2_silu_mi300.cuh
+                             + moe_mul_sum_add) */
+  MK_OP_STREAM = 9        /* read-only bandwidth probe of the weight ring (stream_mi300.cuh:99) */
+};
+
+/* MkOp.flags */
+#define MK_F_NORM (1 << 0)       /* GEMV/GATEUP: RMSNorm prologue on x with ptr w_norm */
+#define MK_F_RESIDUAL (1 << 1)   /* GEMV: add res before the rounding */
+#define MK_F_ARGMAX (1 << 2)     /* GEMV: greedy argmax of the output into tokens[pos + 1] */
+#define MK_F_EXPERT (1 << 3)     /* GATEUP: groups are the routed slots of `mask` */
+
+#define MK_MAX_PTRS 16
+#define MK_MAX_IPARAMS 16
+
+/* One operator. Index meaning per type (MK_P_* / MK_I_* below); unused entries 0. */
+typedef struct MkOp {
+  int32_t type;
+  int32_t flags;
+  int32_t ntasks;          /* 0: the library chooses (one task per CTA or fewer) */
+  int32_t reserved;
+  void* ptr[MK_MAX_PTRS];
+  int64_t ip[MK_MAX_IPARAMS];
+  double fp[4];
+} MkOp;
+
+/* ptr / ip indices per operator type */
+enum { /* MK_OP_EMBED */ MK_P_EMB_W = 0, MK_P_EMB_TOKENS = 1, MK_P_EMB_OUT = 2,
+       MK_I_EMB_V = 0, MK_I_EMB_H = 1 };
+enum { /* MK_OP_GEMV */ MK_P_GEMV_X = 0, MK_P_GEMV_WNORM = 1, MK_P_GEMV_W = 2, MK_P_GEMV_RES = 3,
+       MK_P_GEMV_OUT = 4, MK_P_GEMV_HOUT = 5, MK_P_GEMV_TOKENS = 6,
+       MK_I_GEMV_N = 0, MK_I_GEMV_K = 1, MK_I_GEMV_VOCAB_STRIDE = 2 };
+enum { /* MK_OP_MLA_PREP */ MK_P_PREP_QKVA = 0, MK_P_PREP_WKVNORM = 1, MK_P_PREP_WUKT = 2,
+       MK_P_PREP_COS = 3, MK_P_PREP_SIN = 4, MK_P_PREP_CKV = 5, MK_P_PREP_KPE = 6,
+       MK_P_PREP_QLNOPE = 7, MK_P_PREP_QPE = 8,
+       MK_I_PREP_NH = 0, MK_I_PREP_DN = 1, MK_I_PREP_DR = 2, MK_I_PREP_DC = 3, MK_I_PREP_SMAX = 4 };
+enum { /* MK_OP_MLA_ATTEND */ MK_P_ATT_QLNOPE = 0, MK_P_ATT_QPE = 1, MK_P_ATT_CKV = 2, MK_P_ATT_KPE = 3,
+       MK_P_ATT_PARTIALS = 4,
+       MK_I_ATT_NH = 0, MK_I_ATT_DC = 1, MK_I_ATT_DR = 2, MK_I_ATT_SMAX = 3, MK_I_ATT_SPLIT = 4,
+       MK_I_ATT_HGROUP = 5, MK_I_ATT_NSPLITS = 6, MK_I_ATT_PROW = 7 };
+enum { /* MK_OP_MLA_MERGE_UV */ MK_P_MRG_PARTIALS = 0, MK_P_MRG_WUV = 1, MK_P_MRG_OUT = 2,
+       MK_I_MRG_NH = 0, MK_I_MRG_DV = 1, MK_I_MRG_DC = 2, MK_I_MRG_SPLIT = 3, MK_I_MRG_NSPLITS = 4,
+       MK_I_MRG_PROW = 5 };
+enum { /* MK_OP_ROUTER */ MK_P_RT_X = 0, MK_P_RT_WNORM = 1, MK_P_RT_WGATE = 2, MK_P_RT_HOUT = 3,
+       MK_P_RT_LOGITS = 4, MK_P_RT_TOPKW = 5, MK_P_RT_ROUTING = 6, MK_P_RT_MASK = 7,
+       MK_P_RT_ROUTELOG = 8, MK_P_RT_BIAS = 9,
+       MK_I_RT_H = 0, MK_I_RT_E = 1, MK_I_RT_TOPK = 2, MK_I_RT_NFORCED = 3, MK_I_RT_LAYER = 4,
+       MK_I_RT_LOGSTRIDE = 5, MK_I_RT_LOGROWS = 6 };
+enum { /* MK_OP_GATEUP */ MK_P_GU_X = 0, MK_P_GU_WNORM = 1, MK_P_GU_W = 2, MK_P_GU_MASK = 3,
+       MK_P_GU_MID = 4, MK_P_GU_ACT = 5, MK_P_GU_HOUT = 6,
+       MK_I_GU_K = 0, MK_I_GU_I = 1, MK_I_GU_GROUPS = 2, MK_I_GU_ESTRIDE = 3, MK_I_GU_NEXP = 4 };
+enum { /* MK_OP_W2_COMBINE */ MK_P_W2_ACT = 0, MK_P_W2_W = 1, MK_P_W2_MASK = 2, MK_P_W2_TOPKW = 3,
+       MK_P_W2_XRES = 4, MK_P_W2_OUT8 = 5,
+       MK_I_W2_H = 0, MK_I_W2_I = 1, MK_I_W2_SLOTS = 2, MK_I_W2_ESTRIDE = 3, MK_I_W2_NEXP = 4 };
+enum { /* MK_OP_STREAM */ MK_P_ST_W = 0, MK_P_ST_OUT = 1, MK_I_ST_ROWS = 0, MK_I_ST_K = 1 };
+
+typedef struct MkConfig {
+  int32_t device;            /* CUDA device ordinal */
+  int32_t num_ctas;          /* 0: one per SM */
+  int64_t wait_timeout_ns;   /* bound of every spin (event, stage); 0: 2 s */
+  int32_t trace;             /* 1: record per-task %globaltimer stamps (mk_trace) */
+  int32_t reserved[7];
+} MkConfig;
+
+typedef struct MkStatus {
+  uint32_t error;            /* MK_DERR_* of the first error, 0 if none */
+  uint32_t err_op;           /* operator index of the first error */
+  uint32_t err_task;         /* task index within the operator */
+  uint32_t err_cta;
+  uint32_t err_info;         /* code-specific detail (the awaited event index, the bad id) */
+  uint32_t aborted_ctas;     /* CTAs that left early after an error */
+  uint64_t launches;         /* successful launches so far */
+  uint64_t generation;       /* decode iterations run so far */
+} MkStatus;
+
+typedef struct MkTraceRecord {
+  uint32_t op, task, cta, iter;
+  uint64_t t_ready;          /* the dependency was satisfied (%globaltimer, ns) */
+  uint64_t t_end;            /* the task signalled its event */
+} MkTraceRecord;
+
+typedef struct MkHandle MkHandle;
+
+/* Library ABI version (MK_ABI_VERSION). */
+int mk_version(void);
+/* Last error message of this thread (static storage). */
+const char* mk_last_error(void);
+
+/* Create a handle on cfg->device (replaces init_persistent_kernel's construction part). */
+int mk_create(const MkConfig* cfg, MkHandle** out);
+/* Append one operator; *op_index receives its position in the chain. Operators run in the
+   order added; each waits for the previous one (the reference's chain rule,
+   fleet/graph_plan.py:189-199). */
+int mk_add_op(MkHandle* h, const MkOp* op, int32_t* op_index);
+/* Build the per-CTA schedule and upload it (the reference's compile()). */
+int mk_finalize(MkHandle* h);
+/* Run `iters` decode iterations in ONE kernel launch on `stream` (a cudaStream_t, NULL for the
+   default stream). Iteration i runs at position step + 1 + i: it reads tokens[step + 1 + i]
+   and writes tokens[step + 2 + i]; `meta_step` (int32 device pointer or NULL) receives
+   step + iters when the launch completes (the reference's prepare_next_batch, D14). */
+int mk_launch(MkHandle* h, void* stream, int32_t iters, int32_t step, int32_t* meta_step);
+/* Copy the device status word (synchronises the handle's last stream). MK_EDEVICE if error. */
+int mk_status(MkHandle* h, MkStatus* out);
+/* Clear a device error so the handle can launch again (the events are reset too). */
+int mk_reset(MkHandle* h);
+/* Trace records of the last launch (trace enabled): copies up to cap records, *n = count. */
+int mk_trace(MkHandle* h, MkTraceRecord* out, int64_t cap, int64_t* n);
+/* Schedule introspection: tasks of operator op_index, and the CTA of its task t. */
+int mk_op_tasks(MkHandle* h, int32_t op_index, int32_t* ntasks);
+/* Release everything the library allocated (replaces finalize_persistent_kernel). */
+int mk_destroy(MkHandle* h);
+
+/* Test hook: make operator op_index of the next launch wait for an event that never fires,
+   so the bounded wait runs out and the status reports MK_DERR_WAIT_TIMEOUT (no GPU fault). */
+int mk_debug_block_op(MkHandle* h, int32_t op_index);
+
+/* Self-test of the device's deterministic arithmetic on n values (device pointers):
+   fn 0 det_exp, 1 det_log, 2 silu, 3 bf16_from_f64 (x is double*, out is uint16_t*),
+   4 bf16 round of float (out uint16_t*). */
+int mk_selftest_math(int32_t fn, const void* x, void* out, int64_t n, void* stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLEET_MK_H */

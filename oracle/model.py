@@ -36,6 +36,12 @@ class OracleModel:
     def W_uk(self, l):
         return np.ascontiguousarray(self.get(f"W_ukT_{l}").transpose(0, 2, 1))
 
+    @staticmethod
+    def gate_up(w):
+        """The packed W13 / W_gu interleave gate and up rows (row 2i gate i, 2i+1 up i); the
+        reference's arithmetic reads [gate rows; up rows]."""
+        return np.concatenate([w[0::2], w[1::2]], axis=0)
+
     def attention(self, l, x_res, cache, cos, sin, pos, rec):
         d = self.d
         h, qkva = R.linear_norm(x_res, self.get(f"w_norm1_{l}"), self.get(f"W_qkva_{l}"), self.eps)
@@ -56,7 +62,7 @@ class OracleModel:
     def dense_mlp(self, x_res, rec):
         d = self.d
         h = R.rmsnorm(x_res, self.get("w_norm2_0"), self.eps)
-        mid, act, out = R.dense_mlp(h, self.get("W_gu_0"), self.get("W_down_0"), x_res, d.I_DENSE)
+        mid, act, out = R.dense_mlp(h, self.gate_up(self.get("W_gu_0")), self.get("W_down_0"), x_res, d.I_DENSE)
         if rec is not None:
             rec.update({"L0.norm2": h, "L0.mid": mid, "L0.act": act, "L0.layer_out": out})
         return out
@@ -72,7 +78,7 @@ class OracleModel:
         out8 = np.full((n_slots, d.H), np.nan, F32)
         for s in range(int(mask[-1])):
             e = int(mask[s])
-            mid[s] = R.linear(h, self.get_expert(f"W13_{l}", e))
+            mid[s] = R.linear(h, self.gate_up(self.get_expert(f"W13_{l}", e)))
             act = R.swiglu_act(mid[s], d.I_MOE)
             out8[s] = R.linear(act, self.get_expert(f"W2_{l}", e))
         out = R.moe_combine(out8, topk_w, x_res)

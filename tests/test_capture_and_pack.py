@@ -56,10 +56,12 @@ def test_pack_state_dict_roundtrip(golden):
     assert torch.equal(packed["W_ukT_1"], kvb[:, :d.D_N].transpose(1, 2))
     assert torch.equal(packed["W_uv_1"], kvb[:, d.D_N:])
     sh = sd["model.layers.2.mlp.shared_experts.gate_proj.weight"]
-    assert torch.equal(packed["W13_2"][d.E + 1, :d.I_MOE], sh[d.I_MOE:2 * d.I_MOE])
+    assert torch.equal(packed["W13_2"][d.E + 1, 0::2], sh[d.I_MOE:2 * d.I_MOE])
     assert torch.equal(packed["W2_2"][d.E, :, :], sd["model.layers.2.mlp.shared_experts.down_proj.weight"][:, :d.I_MOE])
-    assert torch.equal(packed["W13_1"][3, d.I_MOE:], sd["model.layers.1.mlp.experts.3.up_proj.weight"])
-    assert torch.equal(packed["W_gu_0"][d.I_DENSE:], sd["model.layers.0.mlp.up_proj.weight"])
+    assert torch.equal(packed["W13_1"][3, 1::2], sd["model.layers.1.mlp.experts.3.up_proj.weight"])
+    assert torch.equal(packed["W_gu_0"][1::2], sd["model.layers.0.mlp.up_proj.weight"])
+    g, u = P.deinterleave_gate_up(packed["W13_1"][5])
+    assert torch.equal(g, sd["model.layers.1.mlp.experts.5.gate_proj.weight"]) and torch.equal(u, sd["model.layers.1.mlp.experts.5.up_proj.weight"])
     total = sum(v.numel() * v.element_size() for v in packed.values())
     assert total == P.packed_bytes(d)
 

@@ -1,0 +1,93 @@
+"""End-to-end parity of the persistent decode graph with the CPU oracle (oracle/model.py).
+
+The graph is built through the reference-shaped surface (fleet/build_graph.build with the packed
+weights, the capture and the meta tensors), runs greedy iterations in one launch, and must give
+the oracle's token ids, route log, cache rows and final residual bit for bit. DeepSeek-V2-Lite
+shapes with a reduced layer count (layer 0 dense + MoE layers + the head) so the oracle finishes
+in seconds; the full 27-layer graph is the bench's workload.
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_helpers import DeviceWeights, assert_bits_equal, np32
+from oracle.detmath import from_bf16_bits
+from oracle.model import OracleModel
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def build_model(layers, iters, n_past=1023, seed=0, random_norms=True, dims=None, split=None):
+    from fleet import build_graph as B
+    from fleet import graph_plan as G
+    from fleet.capture import make_capture
+    from fleet.pack_weights import REAL_DIMS, synthetic_packed
+    d = dims or REAL_DIMS
+    s_max = n_past + 1 + iters          # tokens[n_past + 1 .. n_past + iters] are generated
+    packed = synthetic_packed(d, layers=layers, head=True, seed=seed, device=DEV, random_norms=random_norms)
+    capture = make_capture(d, layers, s_max, n_past, seed=seed + 1, device=DEV)
+    prompt = torch.randint(0, d.V, (n_past + 1,), generator=torch.Generator().manual_seed(seed + 2))
+    meta = B.make_meta(torch, s_max, prompt.tolist(), n_past + 1, device=DEV)
+    cache0 = {k: np32(v) for k, v in capture.items() if k.startswith(("c_kv_", "k_pe_"))}
+    kw = {} if split is None else dict(split=split)
+    mpk, host, plan = B.build(packed, capture, meta, dims=d, s_max=s_max, layers=layers, head=True, **kw)
+    return d, packed, capture, meta, cache0, mpk, host, plan, n_past
+
+
+def oracle_run(d, packed, capture, meta, cache0, plan, layers, iters, pos0):
+    from fleet.capture import softmax_scale
+    dw = DeviceWeights(packed)
+    m = OracleModel(d, dw.get, dw.get_expert, softmax_scale=softmax_scale(d.D_N, d.D_R), split=plan.split,
+                    layers=layers)
+    tokens = meta["tokens"][0].cpu().numpy().copy()
+    cache = {k: v.copy() for k, v in cache0.items()}
+    cos, sin = np32(capture["cos"]), np32(capture["sin"])
+    ids, routes, rec = m.generate(tokens, pos0, iters, cache, cos, sin, record_last=True)
+    return ids, routes, rec, cache
+
+
+@pytest.mark.parametrize("layers,iters", [(3, 4)])
+def test_decode_one_launch_matches_oracle(layers, iters):
+    d, packed, capture, meta, cache0, mpk, host, plan, pos0 = build_model(layers, iters)
+    mpk.compile()
+    meta["step"].fill_(pos0 - 1)
+    mpk()                                                    # every remaining iteration, one launch
+    st = mpk.status()
+    assert st["error"] == 0, st
+    assert int(meta["step"].item()) == pos0 - 1 + (plan.s_max - 2 - (pos0 - 1))
+    n_run = plan.s_max - 2 - (pos0 - 1)
+    ids = meta["tokens"][0, pos0 + 1: pos0 + 1 + n_run].tolist()
+    want_ids, routes, rec, cache = oracle_run(d, packed, capture, meta, cache0, plan, layers, n_run, pos0)
+    assert ids == want_ids
+    rl = host["route_log"].cpu().numpy()
+    for i in range(n_run):
+        for l in range(1, layers):
+            assert rl[i, l - 1, :d.TOPK].tolist() == routes[i][l - 1], (i, l)
+    for l in range(layers):
+        got = host[f"c_kv_{l}"][pos0:pos0 + n_run].float().cpu().numpy()
+        assert np.array_equal(got, cache[f"c_kv_{l}"][pos0:pos0 + n_run]), l
+        got = host[f"k_pe_{l}"][pos0:pos0 + n_run].float().cpu().numpy()
+        assert np.array_equal(got, cache[f"k_pe_{l}"][pos0:pos0 + n_run]), l
+    # the last iteration's workspaces: the final residual, the logits and the last layer's router
+    assert_bits_equal(host["logits"][0], rec["head.logits"], "logits")
+    assert_bits_equal(host["h"][0], rec["head.norm"], "final norm")
+    L = layers - 1
+    assert np.array_equal(host["mask"].cpu().numpy(), rec[f"L{L}.mask"])
+    assert_bits_equal(host["out8"], rec[f"L{L}.out8"], "out8")
+
+
+def test_decode_launch_per_token_equals_one_launch():
+    """Three launches of one iteration give the same ids and state as one launch of three."""
+    layers, iters = 2, 3
+    d, packed, capture, meta, cache0, mpk, host, plan, pos0 = build_model(layers, iters, seed=5)
+    mpk.compile()
+    mpk.step = pos0 - 1
+    for _ in range(plan.s_max - 2 - (pos0 - 1)):
+        mpk.launch(1)
+    assert mpk.status()["error"] == 0
+    n_run = plan.s_max - 2 - (pos0 - 1)
+    ids = meta["tokens"][0, pos0 + 1: pos0 + 1 + n_run].tolist()
+    want_ids, _, rec, _ = oracle_run(d, packed, capture, meta, cache0, plan, layers, n_run, pos0)
+    assert ids == want_ids
+    assert_bits_equal(host["logits"][0], rec["head.logits"], "logits")
