@@ -181,6 +181,23 @@ int mk_debug_block_op(MkHandle* h, int32_t op_index);
    4 bf16 round of float (out uint16_t*). */
 int mk_selftest_math(int32_t fn, const void* x, void* out, int64_t n, void* stream);
 
+/* MLA decode attention without any device allocation. There is no counterpart in the reference;
+   it exists for callers that cannot call cudaMalloc where they call this (an engine that owns all
+   of HBM through its own pool, code running under the caller's allocator lock, loops that cannot
+   take cudaMalloc's implicit synchronisation). It computes what the persistent kernel's
+   MK_OP_MLA_ATTEND + MK_OP_MLA_MERGE_UV compute at position `pos`, bit for bit:
+   attn_out[nh * d_v] = merge of the ceil((pos + 1) / split) live splits, times W_uv.
+   Inputs (device, BF16): ql_nope [nh, d_c], q_pe [nh, d_r], c_kv [>= pos + 1, d_c],
+   k_pe [>= pos + 1, d_r], w_uv [nh, d_v, d_c]. The split-KV partials live in a file-scope
+   __device__ array of 2 MiB (64 splits x 16 heads x 516 floats) that each GPU keeps until the
+   process exits: limits nh <= 16, d_c <= 512 (a multiple of 32), d_r <= 64 (even), split <= 256,
+   and ceil((pos + 1) / split) <= 64; anything beyond returns MK_EINVAL. The first call on a
+   device looks up that array's device address (cudaGetSymbolAddress) and should come before any
+   stream capture. All calls share the array: calls that overlap on the GPU race. */
+int mk_mla_decode_noalloc(const void* ql_nope, const void* q_pe, const void* c_kv, const void* k_pe,
+                          const void* w_uv, void* attn_out, int32_t nh, int32_t d_c, int32_t d_r, int32_t d_v,
+                          int32_t pos, int32_t split, float softmax_scale, void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif
