@@ -3,9 +3,9 @@
 // the shared-memory ring, issued by the producer warp) and a consumer half (what the eight
 // consumer warps compute from those stages and from activations in L2).
 //
-// Arithmetic contract (oracle/numpy_ref.py is the CPU statement of it): every dot product of
-// BF16 values accumulates exact products in FP64 (any order) and is rounded once; every exp/log
-// is det_exp/det_log; the rounding points are the reference's (harness/numpy_ref.py:36-321).
+// Arithmetic contract (oracle/numpy_ref.py is the CPU statement of it): every sum is FP32 in the
+// order oracle/detmath.py specifies (row dot, butterfly, block / lane / sequential sums); every
+// exp/log is det_exp/det_log; the rounding points are the reference's (harness/numpy_ref.py:36-321).
 #pragma once
 #include "mk_device.cuh"
 
@@ -22,7 +22,17 @@ struct Iter {
 struct Cons {       // consumer-side state
   uint32_t c_it, c_rel;
   int warp, lane, tid;
+  bool trace;                           // record the stamps below (thread 0 only)
+  uint64_t t_body, t_stages, wait_ns;
 };
+
+// trace stamps of the task body: activations loaded / last weight stage consumed
+__device__ __forceinline__ void mark_body(Cons& c) {
+  if (c.trace && c.tid == 0) c.t_body = globaltimer();
+}
+__device__ __forceinline__ void mark_stages(Cons& c) {
+  if (c.trace && c.tid == 0) c.t_stages = globaltimer();
+}
 
 // ---- error reporting ------------------------------------------------------------------------
 
@@ -76,11 +86,14 @@ __device__ __noinline__ bool ring_wait(const KernelParams& P, Smem& sm, uint64_t
 __device__ __forceinline__ uint8_t* acquire_stage(const KernelParams& P, Smem& sm, Cons& c, uint32_t op,
                                                   uint32_t task) {
   const uint32_t st = c.c_it % NSTAGES, ph = (c.c_it / NSTAGES) & 1u;
-  if (!*(volatile uint32_t*)&sm.cta_abort && !ring_wait(P, sm, &sm.full[st], ph)) {
+  const uint64_t t0 = (c.trace && c.tid == 0) ? globaltimer() : 0;
+  if (!mbar_try_wait(&sm.full[st], ph) && !*(volatile uint32_t*)&sm.cta_abort &&
+      !ring_wait(P, sm, &sm.full[st], ph)) {
     if (c.lane == 0)
       report_error(P, sm, *(volatile uint32_t*)&P.status->abort_flag ? MK_DERR_ABORTED : MK_DERR_RING_TIMEOUT,
                    op, task, 1);
   }
+  if (c.trace && c.tid == 0) c.wait_ns += globaltimer() - t0;
   c.c_it++;
   return sm.ring[st];
 }
@@ -92,57 +105,51 @@ __device__ __forceinline__ void release_stage(Smem& sm, Cons& c) {
   if (c.lane == 0) mbar_arrive(&sm.empty[st]);
 }
 
-// ---- FP64 exact dot products ----------------------------------------------------------------
+// ---- FP32 dot products in the specified order -------------------------------------------------
 
-// x' (activation scaled by 2^832) for vectors v = lane + 32 j of a K-slice; x is BF16 bits.
+// x for vectors v = lane + 32 j of a K-slice, as FP32 registers; x is BF16 bits.
 template <int MAXV, bool SMEM>
-__device__ __forceinline__ void load_x(double (&xr)[MAXV][8], const uint16_t* x, int klen, int lane) {
+__device__ __forceinline__ void load_x(float (&xr)[MAXV][8], const uint16_t* x, int klen, int lane) {
 #pragma unroll
   for (int j = 0; j < MAXV; ++j) {
     const int v = lane + 32 * j;
     uint4 raw = make_uint4(0u, 0u, 0u, 0u);
     if (v * 8 < klen) raw = SMEM ? *reinterpret_cast<const uint4*>(x + v * 8) : ldcg16(x + v * 8);
-    xr[j][0] = xprime(bf16_bits_to_f32(raw.x & 0xFFFFu));
-    xr[j][1] = xprime(bf16_bits_to_f32(raw.x >> 16));
-    xr[j][2] = xprime(bf16_bits_to_f32(raw.y & 0xFFFFu));
-    xr[j][3] = xprime(bf16_bits_to_f32(raw.y >> 16));
-    xr[j][4] = xprime(bf16_bits_to_f32(raw.z & 0xFFFFu));
-    xr[j][5] = xprime(bf16_bits_to_f32(raw.z >> 16));
-    xr[j][6] = xprime(bf16_bits_to_f32(raw.w & 0xFFFFu));
-    xr[j][7] = xprime(bf16_bits_to_f32(raw.w >> 16));
+    xr[j][0] = lo_f32(raw.x);
+    xr[j][1] = hi_f32(raw.x);
+    xr[j][2] = lo_f32(raw.y);
+    xr[j][3] = hi_f32(raw.y);
+    xr[j][4] = lo_f32(raw.z);
+    xr[j][5] = hi_f32(raw.z);
+    xr[j][6] = lo_f32(raw.w);
+    xr[j][7] = hi_f32(raw.w);
   }
 }
 
-// One BF16 row (in shared memory) against x'; the warp-reduced exact dot product (all lanes).
+// One BF16 row part (in shared memory) against x: lane l adds its vectors v = l + 32 j in order,
+// value t of a vector into a0 (t even) or a1 (t odd); then a0 + a1 and the butterfly. Every
+// product of BF16 values is exact, so fmaf is the rounded add. All lanes return the part sum.
 template <int MAXV>
-__device__ __forceinline__ double row_dot(const double (&xr)[MAXV][8], const uint8_t* row, int klen, int lane) {
-  double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+__device__ __forceinline__ float row_dot(const float (&xr)[MAXV][8], const uint8_t* row, int klen, int lane) {
+  float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
   for (int j = 0; j < MAXV; ++j) {
     const int v = lane + 32 * j;
     if (v * 8 < klen) {
       const uint4 w = *reinterpret_cast<const uint4*>(row + v * 16);
-      a0 = fma(wlo_f64(w.x), xr[j][0], a0);
-      a1 = fma(whi_f64(w.x), xr[j][1], a1);
-      a2 = fma(wlo_f64(w.y), xr[j][2], a2);
-      a3 = fma(whi_f64(w.y), xr[j][3], a3);
-      a0 = fma(wlo_f64(w.z), xr[j][4], a0);
-      a1 = fma(whi_f64(w.z), xr[j][5], a1);
-      a2 = fma(wlo_f64(w.w), xr[j][6], a2);
-      a3 = fma(whi_f64(w.w), xr[j][7], a3);
+      a0 = fmaf(lo_f32(w.x), xr[j][0], a0);
+      a1 = fmaf(hi_f32(w.x), xr[j][1], a1);
+      a0 = fmaf(lo_f32(w.y), xr[j][2], a0);
+      a1 = fmaf(hi_f32(w.y), xr[j][3], a1);
+      a0 = fmaf(lo_f32(w.z), xr[j][4], a0);
+      a1 = fmaf(hi_f32(w.z), xr[j][5], a1);
+      a0 = fmaf(lo_f32(w.w), xr[j][6], a0);
+      a1 = fmaf(hi_f32(w.w), xr[j][7], a1);
     }
   }
-  double a = (a0 + a1) + (a2 + a3);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-  return a * DOT_UNSCALE;
+  return warp_butterfly(__fadd_rn(a0, a1));
 }
 
-__device__ __forceinline__ double warp_sum_f64(double a) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-  return a;
-}
 __device__ __forceinline__ float warp_max_f32(float a) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
@@ -150,27 +157,55 @@ __device__ __forceinline__ float warp_max_f32(float a) {
 }
 
 // ---- RMSNorm of a BF16 row into shared memory (all 256 consumer threads) ----------------------
-// h = bf16(w * bf16(x * r)), r = 1 / sqrt(f32(exact sum x^2 / K) + eps)   (numpy_ref.py:54-60)
+// h = bf16(w * bf16(x * r)), r = 1 / sqrt(ss / K + eps)   (numpy_ref.py:54-60), with ss the FP32
+// sum of squares in the block order: thread t adds the 8-value vectors t, t + 256, ... in order,
+// the warps reduce by the butterfly, and warps 0..7 are added in order (oracle detmath.block_sum).
+constexpr int NORM_MAX_VECS = 2;   // K <= 4096
 __device__ void rmsnorm_to_smem(const uint16_t* x, const uint16_t* w, int K, float eps, uint16_t* hbuf, Smem& sm,
                                 const Cons& c) {
-  double ss = 0.0;
-  for (int i = c.tid; i < K; i += NUM_CONSUMERS) {
-    const double v = (double)bf16_bits_to_f32(ldcg_u16(x + i));
-    ss = fma(v, v, ss);
-  }
-  ss = warp_sum_f64(ss);
-  if (c.lane == 0) sm.red[c.warp] = ss;
-  consumer_sync();
-  double tot = 0.0;
+  // one pass over global memory: a thread's 16-byte vectors are loaded together
+  const int nv = K / 8;
+  uint4 xv[NORM_MAX_VECS], wv[NORM_MAX_VECS];
 #pragma unroll
-  for (int k = 0; k < NUM_CONSUMER_WARPS; ++k) tot += sm.red[k];
-  const float var = __double2float_rn(tot / (double)K);
+  for (int k = 0; k < NORM_MAX_VECS; ++k) {
+    const int v = c.tid + k * NUM_CONSUMERS;
+    xv[k] = v < nv ? ldcg16(x + (size_t)v * 8) : make_uint4(0u, 0u, 0u, 0u);
+    wv[k] = v < nv ? __ldg(reinterpret_cast<const uint4*>(w) + v) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NORM_MAX_VECS; ++k) {
+    if (c.tid + k * NUM_CONSUMERS < nv) {
+      const uint32_t u[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        ss = fmaf(lo_f32(u[q]), lo_f32(u[q]), ss);
+        ss = fmaf(hi_f32(u[q]), hi_f32(u[q]), ss);
+      }
+    }
+  }
+  ss = warp_butterfly(ss);
+  float* red = reinterpret_cast<float*>(sm.red);
+  if (c.lane == 0) red[c.warp] = ss;
+  consumer_sync();
+  float tot = red[0];
+#pragma unroll
+  for (int k = 1; k < NUM_CONSUMER_WARPS; ++k) tot = __fadd_rn(tot, red[k]);
+  const float var = __fdiv_rn(tot, (float)K);
   const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-  for (int i = c.tid; i < K; i += NUM_CONSUMERS) {
-    const float v = bf16_bits_to_f32(ldcg_u16(x + i));
-    const float xn = round_bf16(__fmul_rn(v, r));
-    const float wv = bf16_bits_to_f32(__ldg(w + i));
-    hbuf[i] = (uint16_t)f32_to_bf16_bits(__fmul_rn(wv, xn));
+  auto nrm = [&](float xe, float we) -> uint32_t { return f32_to_bf16_bits(__fmul_rn(we, round_bf16(__fmul_rn(xe, r)))); };
+#pragma unroll
+  for (int k = 0; k < NORM_MAX_VECS; ++k) {
+    const int v = c.tid + k * NUM_CONSUMERS;
+    if (v < nv) {
+      const uint32_t ux[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+      const uint32_t uw[4] = {wv[k].x, wv[k].y, wv[k].z, wv[k].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        o[q] = nrm(lo_f32(ux[q]), lo_f32(uw[q])) | (nrm(hi_f32(ux[q]), hi_f32(uw[q])) << 16);
+      reinterpret_cast<uint4*>(hbuf)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
   consumer_sync();   // hbuf complete; sm.red free again
 }

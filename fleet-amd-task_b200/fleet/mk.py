@@ -60,7 +60,8 @@ class MkStatus(ctypes.Structure):
 
 class MkTraceRecord(ctypes.Structure):
     _fields_ = [("op", ctypes.c_uint32), ("task", ctypes.c_uint32), ("cta", ctypes.c_uint32),
-                ("iter", ctypes.c_uint32), ("t_ready", ctypes.c_uint64), ("t_end", ctypes.c_uint64)]
+                ("iter", ctypes.c_uint32), ("t_ready", ctypes.c_uint64), ("t_end", ctypes.c_uint64),
+                ("t_body", ctypes.c_uint64), ("t_stages", ctypes.c_uint64), ("wait_ns", ctypes.c_uint64)]
 
 
 EXPORTS = ["mk_version", "mk_last_error", "mk_create", "mk_add_op", "mk_finalize", "mk_launch", "mk_status",
@@ -193,7 +194,7 @@ class MegaKernel:
         m = min(n.value, cap)
         buf = (MkTraceRecord * max(1, m))()
         _check(lib().mk_trace(self.h, buf, m, ctypes.byref(n)), "mk_trace")
-        return [(r.op, r.task, r.cta, r.iter, r.t_ready, r.t_end) for r in buf[:m]]
+        return [(r.op, r.task, r.cta, r.iter, r.t_ready, r.t_end, r.t_body, r.t_stages, r.wait_ns) for r in buf[:m]]
 
     def close(self):
         if getattr(self, "h", None):

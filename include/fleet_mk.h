@@ -139,6 +139,9 @@ typedef struct MkTraceRecord {
   uint32_t op, task, cta, iter;
   uint64_t t_ready;          /* the dependency was satisfied (%globaltimer, ns) */
   uint64_t t_end;            /* the task signalled its event */
+  uint64_t t_body;           /* the task's prologue (activations loaded) was done, 0 if none */
+  uint64_t t_stages;         /* its last weight stage was consumed, 0 if none */
+  uint64_t wait_ns;          /* time its consumer warp 0 spent waiting for weight stages */
 } MkTraceRecord;
 
 typedef struct MkHandle MkHandle;

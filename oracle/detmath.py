@@ -10,11 +10,10 @@ is not specified", numpy_ref.py:18-20) and the implementation of exp/log. Both m
 oracle and a GPU kernel disagree in the last bit, and a last-bit difference in a BF16
 rounding can flip a router choice or a greedy token. This restatement closes both:
 
-* every dot product of BF16 values is computed exactly (the products are exact in FP64 and
-  the FP64 sum of at most a few thousand of them is exact to 2^-53) and rounded ONCE, to
-  FP32 or straight to BF16; the kernels accumulate in FP64 too, so any summation order gives
-  the same rounded value (they differ only if the exact sum lies within ~1e-16 relative of a
-  rounding midpoint);
+* every dot product of BF16 values is an FP32 sum of exact products in ONE specified order
+  (below: dot_rows, block_sum, lane_sum, seq_sum), the order the kernels use, so the CPU
+  reproduces the kernels' bits (the reference's NumPy sums in BLAS order; the two agree within
+  the reference's own kernel tolerances);
 * exp and log are the two routines below, made of separately rounded FP32 operations (no
   fused multiply-add), which IEEE-754 makes bit-identical on any machine. The kernels use
   ``__fmul_rn``/``__fadd_rn``/``__fsub_rn``/``__fdiv_rn``, which the compiler never contracts.
@@ -47,17 +46,10 @@ SQRT2 = F32(math.sqrt(2.0))
 EXP_LO = F32(-87.0)      # below: result 0 (true value < 2^-125, flushed)
 EXP_HI = F32(88.0)       # above: +inf (true value > 1.6e38)
 
-# the exponent field offsets of the FP64 "bit placement" trick used by the kernels to turn a
-# BF16 pattern into an FP64 scaled by 2^-896 without a conversion instruction; the activation
-# operand is pre-scaled by 2^832 so every product carries 2^-64, undone once per dot product
-BF16_F64_SHIFT = 45
-W_SCALE_LOG2 = -896
-X_SCALE_LOG2 = 832
-DOT_UNSCALE_LOG2 = 64
 
 
 def _f32(x):
-    return np.ascontiguousarray(np.asarray(x, dtype=F32))
+    return np.require(np.asarray(x, dtype=F32), requirements="C")      # keeps 0-d scalars 0-d
 
 
 # ---------------------------------------------------------------------------------------------
@@ -110,17 +102,126 @@ def from_bf16_bits(b):
 
 
 # ---------------------------------------------------------------------------------------------
-# exact dot products
+# the kernels' FP32 summation orders
+#
+# Every product of two BF16 values is exact in FP32, so an FP32 dot product of BF16 vectors is
+# determined by the ORDER of its additions alone. The kernels fix that order and the functions
+# below reproduce it operation for operation (numpy's float32 `+` is the same IEEE add):
+#
+#   row dot (GEMV):  the row is cut into KS parts of kp = K / KS values (KS 1 for K <= 1024,
+#     2 for K <= 2048, else 8); in a part, lane l (of 32) takes the 8-value vectors
+#     v = l + 32 j, j < MAXV = ceil(kp / 256), and adds their products in the order
+#     (j, t = 0..7) into two accumulators, a0 for even t and a1 for odd t; a lane's value is
+#     a0 + a1; the 32 lane values are combined by the butterfly a_l <- a_l + a_(l xor o) for
+#     o = 16, 8, 4, 2, 1; the parts are then added in part order.
+#   column sums (attention P.V, merge): sequential over the rows / splits, row 0 first.
+#   block sums (RMSNorm): thread t adds the 8-value vectors t, t + 256, ... in order, butterfly
+#     over the warp, then the warps in order.
+#   lane sums (softmax denominators): lane l adds elements l, l + 32, ... in order, then the
+#     butterfly.
+#   attention scores: lane l adds the products of its contiguous latent columns, then of its
+#     contiguous rope columns, into one accumulator, then the butterfly.
 
 
-def dot_exact(W, x):
-    """Rows of W (BF16 values) against x (BF16 or FP32 values), every product exact, summed in
-    FP64. Returns FP64; the caller rounds once (bf16_from_f64 or f32_from_f64)."""
-    return np.asarray(W, F64) @ np.asarray(x, F64)
+def gemv_parts(K):
+    """(KS, kp, MAXV) of a row of K values, as the kernels choose them."""
+    ks = 1 if K <= 1024 else (2 if K <= 2048 else 8)
+    assert K % (8 * ks) == 0, (K, ks)
+    kp = K // ks
+    return ks, kp, -(-kp // 256)
 
 
-def sum_f64(x, axis=-1):
-    return np.sum(np.asarray(x, F64), axis=axis)
+def butterfly(a):
+    """The xor-shuffle reduction over the last axis (32 lanes): every lane ends with the total."""
+    lanes = np.arange(32)
+    for o in (16, 8, 4, 2, 1):
+        a = (a + a[..., lanes ^ o]).astype(F32)
+    return a[..., 0]
+
+
+def dot_rows(W, x):
+    """FP32 dot products of the rows of W [..., N, K] with x [K] in the kernels' order.
+    W and x hold BF16 values (so each product is exact). Returns float32 [..., N]."""
+    W = np.asarray(W, F32)
+    x = np.asarray(x, F32)
+    K = W.shape[-1]
+    ks, kp, maxv = gemv_parts(K)
+    lead = W.shape[:-1]
+    pad = maxv * 256 - kp
+    Wp = W.reshape(*lead, ks, kp)
+    xp = x.reshape(ks, kp)
+    if pad:
+        Wp = np.concatenate([Wp, np.zeros((*lead, ks, pad), F32)], axis=-1)
+        xp = np.concatenate([xp, np.zeros((ks, pad), F32)], axis=-1)
+    Wp = Wp.reshape(*lead, ks, maxv, 32, 8)
+    xp = xp.reshape(ks, maxv, 32, 8)
+    valid = (np.arange(maxv)[:, None] * 32 + np.arange(32)[None, :]) * 8 < kp       # [maxv, 32]
+    a0 = np.zeros((*lead, ks, 32), F32)
+    a1 = np.zeros((*lead, ks, 32), F32)
+    for j in range(maxv):
+        vj = valid[j]
+        for t in range(8):
+            prod = (Wp[..., j, :, t] * xp[:, j, :, t]).astype(F32)
+            if t % 2 == 0:
+                a0 = np.where(vj, (a0 + prod).astype(F32), a0)
+            else:
+                a1 = np.where(vj, (a1 + prod).astype(F32), a1)
+    parts = butterfly((a0 + a1).astype(F32))                                         # [..., N, ks]
+    d = parts[..., 0]
+    for p in range(1, ks):
+        d = (d + parts[..., p]).astype(F32)
+    return d
+
+
+def block_sum(v, threads=256, warps=8, vec=8):
+    """Sum of the last axis (a multiple of 8 long) as a 256-thread block adds it: thread t takes
+    the 8-value vectors t, t + 256, ... and adds their values in order, each warp reduces by the
+    butterfly, then warps 0..7 are added in order."""
+    v = np.asarray(v, F32)
+    n = v.shape[-1]
+    assert n % vec == 0, n
+    nv = n // vec
+    per = -(-nv // threads)
+    pad = per * threads * vec - n
+    if pad:
+        v = np.concatenate([v, np.zeros((*v.shape[:-1], pad), F32)], axis=-1)
+    v = v.reshape(*v.shape[:-1], per, threads, vec)
+    acc = np.zeros((*v.shape[:-3], threads), F32)
+    for i in range(per):
+        valid = i * threads + np.arange(threads) < nv
+        for e in range(vec):
+            acc = np.where(valid, (acc + v[..., i, :, e]).astype(F32), acc)
+    w = butterfly(acc.reshape(*acc.shape[:-1], warps, 32))                              # [..., 8]
+    tot = w[..., 0]
+    for k in range(1, warps):
+        tot = (tot + w[..., k]).astype(F32)
+    return tot
+
+
+def lane_sum(v):
+    """Sum of the last axis as one warp adds it: lane l takes elements l, l + 32, ... in order,
+    then the butterfly."""
+    v = np.asarray(v, F32)
+    n = v.shape[-1]
+    per = -(-n // 32)
+    pad = per * 32 - n
+    if pad:
+        v = np.concatenate([v, np.zeros((*v.shape[:-1], pad), F32)], axis=-1)
+    v = v.reshape(*v.shape[:-1], per, 32)
+    acc = np.zeros((*v.shape[:-2], 32), F32)
+    for i in range(per):
+        valid = i * 32 + np.arange(32) < n
+        acc = np.where(valid, (acc + v[..., i, :]).astype(F32), acc)
+    return butterfly(acc)
+
+
+def seq_sum(v, axis=0):
+    """Sequential FP32 sum along `axis`, first element first."""
+    v = np.moveaxis(np.asarray(v, F32), axis, 0)
+    acc = np.zeros(v.shape[1:], F32)
+    for i in range(v.shape[0]):
+        acc = (acc + v[i]).astype(F32)
+    return acc
 
 
 # ---------------------------------------------------------------------------------------------

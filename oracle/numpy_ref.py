@@ -8,16 +8,16 @@ thing measured or shipped. Only ``tests/``, ``__graft_entry__.smoke()`` and ``be
 
 Rounding points are the reference's (BF16 wherever the reference stores BF16 or feeds a BF16
 matrix operand); the two freedoms the reference leaves open are closed as ``oracle.detmath``
-explains: every dot product is exact and rounded once, and exp/log are deterministic routines.
-So the CUDA kernels, which make the same choices, must agree bit for bit, and the reference's
-own functions agree within their own tolerances (tests/test_oracle_pins.py checks both).
+explains: every FP32 sum runs in the kernels' specified order, and exp/log are deterministic
+routines. So the CUDA kernels must agree bit for bit, and the reference's own functions agree
+within their own tolerances (tests/test_oracle_pins.py checks both).
 
 Array conventions: BF16 tensors are float32 arrays holding BF16 values (as numpy_ref does).
 """
 import numpy as np
 
-from oracle.detmath import (F32, F64, bf16, bf16_from_f64, det_exp, det_log, dot_exact,
-                            f32_from_f64, silu, sum_f64)
+from oracle.detmath import (F32, F64, bf16, block_sum, butterfly, det_exp, det_log, dot_rows, lane_sum,
+                            seq_sum, silu)
 
 __all__ = ["bf16", "rmsnorm", "rope", "mla_prep", "mla_attend", "merge_partials", "mla_merge_uv",
            "moe_router", "moe_router_norm", "moe_w13", "moe_w2", "silu", "linear", "linear_norm",
@@ -37,11 +37,11 @@ def partials_row(d_c):
 
 def rmsnorm(x, w, eps=1e-6):
     """DeepseekV2RMSNorm on BF16 inputs (numpy_ref.py:54-60; modeling_deepseek.py:94-108).
-    The sum of squares is exact (FP64), the mean rounded once to FP32; then FP32
-    1/sqrt(var + eps), the normalised value rounded to BF16, times the BF16 weight, rounded."""
+    FP32 sum of squares in the 256-thread block order (detmath.block_sum), divided by n; then
+    FP32 1/sqrt(var + eps), the normalised value rounded to BF16, times the BF16 weight, rounded."""
     x = np.asarray(x, F32)
     n = x.shape[-1]
-    var = f32_from_f64(sum_f64(x.astype(F64) ** 2) / n)[..., None]
+    var = (block_sum((x * x).astype(F32)) / F32(n)).astype(F32)[..., None]
     r = (F32(1.0) / np.sqrt((var + F32(eps)).astype(F32))).astype(F32)
     xn = bf16((x * r).astype(F32))
     return bf16((np.asarray(w, F32) * xn).astype(F32))
@@ -65,13 +65,13 @@ def rope(x, cos_row, sin_row):
 
 
 def linear(x, W):
-    """bf16(W x): exact products, one rounding (numpy_ref.py:304-307)."""
-    return bf16_from_f64(dot_exact(W, x))
+    """bf16(W x): FP32 accumulation in the kernels' order, one rounding (numpy_ref.py:304-307)."""
+    return bf16(dot_rows(W, x))
 
 
 def linear_residual(x, W, res):
-    """bf16(W x + res), the residual added before the one rounding (numpy_ref.py:310-313)."""
-    return bf16_from_f64(dot_exact(W, x) + np.asarray(res, F64))
+    """bf16(W x + res), the residual added in FP32 before the one rounding (numpy_ref.py:310-313)."""
+    return bf16((dot_rows(W, x) + np.asarray(res, F32)).astype(F32))
 
 
 def linear_norm(x, w_norm, W, eps=1e-6):
@@ -98,8 +98,35 @@ def mla_prep(qkva, w_kv_norm, W_uk, cos_row, sin_row, *, nh=16, d_n=128, d_r=64,
     k_pe_row = rope(k_pe_raw, cos_row, sin_row)
     q_nope, q_pe = q[:, :d_n], q[:, d_n:]
     q_pe = rope(q_pe, cos_row, sin_row)
-    ql = np.einsum("hn,hnc->hc", q_nope.astype(F64), np.asarray(W_uk, F64))
-    return c_row, k_pe_row, bf16_from_f64(ql), q_pe
+    W_uk = np.asarray(W_uk, F32)
+    ql = np.stack([dot_rows(W_uk[h].T, q_nope[h]) for h in range(nh)])
+    return c_row, k_pe_row, bf16(ql), q_pe
+
+
+def score_lanes(d):
+    """Columns per lane of a d-wide score operand: d / 32 contiguous columns when d >= 32 (lane l
+    takes [l*n, l*n + n)), else one column for lanes l < d."""
+    return max(1, d // 32)
+
+
+def _scores(ql_nope_h, q_pe_h, c_rows, k_rows):
+    """One head's FP32 scores against cache rows, in the kernels' order: lane l adds the products
+    of its contiguous latent columns [l*LC, l*LC + LC) in order, then of its contiguous rope
+    columns [l*RP, l*RP + RP), into one accumulator; then the butterfly. Products of BF16 values
+    are exact. (d_c is a multiple of 32; d_r is a multiple of 32 or below it.)"""
+    rows = c_rows.shape[0]
+    acc = np.zeros((rows, 32), F32)
+    lanes = np.arange(32)
+    for cols, q in ((c_rows, ql_nope_h), (k_rows, q_pe_h)):
+        d = cols.shape[1]
+        n = score_lanes(d)
+        for m in range(n):
+            col = lanes * n + m
+            ok = col < d
+            cc = np.minimum(col, d - 1)
+            prod = (cols[:, cc] * q[cc]).astype(F32)
+            acc = np.where(ok, (acc + prod).astype(F32), acc)
+    return butterfly(acc)
 
 
 def mla_attend(ql_nope, q_pe, c_kv, k_pe, step, softmax_scale, *, split=32, n_splits=None,
@@ -107,13 +134,13 @@ def mla_attend(ql_nope, q_pe, c_kv, k_pe, step, softmax_scale, *, split=32, n_sp
     """Split-KV attention over cache rows [0, step] (numpy_ref.py:110-149).
 
     Per split j (rows [j*split, min(j*split+split, step+1))) and head h:
-      s = f32(exact ql_nope.c_kv + q_pe.k_pe) * f32(scale)
-      m = max s;  p = det_exp(s - m);  l = f32(exact sum p)
-      o = f32(exact sum bf16(p) c_kv) / l;  lse = m + det_log(l)
+      s = (FP32 q.k in the kernels' order) * f32(scale)
+      m = max s;  p = det_exp(s - m);  l = FP32 sum of p (one warp: lanes then butterfly)
+      o = (FP32 sum over rows, in row order, of bf16(p) c_kv) / l;  lse = m + det_log(l)
     An empty split stores o = 0 and lse = -inf. Returns partials [n_splits, nh, d_c + 1] FP32
     (and the scaled scores [nh, step + 1] with debug_scores)."""
-    ql_nope = np.asarray(ql_nope, F64)
-    q_pe = np.asarray(q_pe, F64)
+    ql_nope = np.asarray(ql_nope, F32)
+    q_pe = np.asarray(q_pe, F32)
     c_kv = np.asarray(c_kv, F32)
     k_pe = np.asarray(k_pe, F32)
     nh, d_c = ql_nope.shape
@@ -127,22 +154,23 @@ def mla_attend(ql_nope, q_pe, c_kv, k_pe, step, softmax_scale, *, split=32, n_sp
         if lo > step:
             partials[j, :, d_c] = -np.inf
             continue
-        s64 = ql_nope @ c_kv[lo:hi].astype(F64).T + q_pe @ k_pe[lo:hi].astype(F64).T
-        s = (f32_from_f64(s64) * scale).astype(F32)
-        if debug_scores:
-            scores_all[:, lo:hi] = s
-        m = s.max(axis=1)
-        p = det_exp((s - m[:, None]).astype(F32))
-        l = f32_from_f64(sum_f64(p, axis=1))
-        acc = bf16(p).astype(F64) @ c_kv[lo:hi].astype(F64)
-        partials[j, :, :d_c] = (f32_from_f64(acc) / l[:, None]).astype(F32)
-        partials[j, :, d_c] = (m + det_log(l)).astype(F32)
+        for h in range(nh):
+            s = (_scores(ql_nope[h], q_pe[h], c_kv[lo:hi], k_pe[lo:hi]) * scale).astype(F32)
+            if debug_scores:
+                scores_all[h, lo:hi] = s
+            m = s.max()
+            p = det_exp((s - m).astype(F32))
+            l = lane_sum(p)
+            acc = seq_sum((bf16(p)[:, None] * c_kv[lo:hi]).astype(F32), axis=0)
+            partials[j, h, :d_c] = (acc / l).astype(F32)
+            partials[j, h, d_c] = (m + det_log(l)).astype(F32)
     return (partials, scores_all) if debug_scores else partials
 
 
 def merge_partials(partials, step, *, split=32, d_c=None):
     """Merge of the live splits (numpy_ref.py:152-165): M = max lse, w_j = det_exp(lse_j - M),
-    o = f32(exact sum w_j o_j / exact sum w_j). d_c: the logical width when rows are padded."""
+    o = (sum_j f32(w_j o_j)) / (sum_j w_j), both sums sequential over j in FP32.
+    d_c: the logical width when rows are padded."""
     if d_c is None:
         d_c = partials.shape[2] - 1
     live = -(-(step + 1) // split)
@@ -150,17 +178,19 @@ def merge_partials(partials, step, *, split=32, d_c=None):
     M = lse.max(axis=0)
     with np.errstate(invalid="ignore"):
         w = det_exp((lse - M[None, :]).astype(F32))                    # [live, nh]
-    num = np.einsum("jh,jhc->hc", w.astype(F64), np.asarray(partials[:live, :, :d_c], F64))
-    den = np.sum(w.astype(F64), axis=0)
-    return f32_from_f64(num / den[:, None])
+    o = np.asarray(partials[:live, :, :d_c], F32)
+    num = seq_sum((w[:, :, None] * o).astype(F32), axis=0)
+    den = seq_sum(w, axis=0)
+    return (num / den[:, None]).astype(F32)
 
 
 def mla_merge_uv(partials, W_uv, step, *, split=32, d_c=None):
-    """attn [nh * d_v]: per head the merge, o rounded to BF16, then bf16(o[h] @ W_uv[h]^T)
+    """attn [nh * d_v]: per head the merge, o rounded to BF16, then bf16(W_uv[h] o[h])
     (numpy_ref.py:168-174)."""
     o = bf16(merge_partials(partials, step, split=split, d_c=d_c))
-    attn = np.einsum("hc,hvc->hv", o.astype(F64), np.asarray(W_uv, F64))
-    return bf16_from_f64(attn.reshape(-1))
+    W_uv = np.asarray(W_uv, F32)
+    attn = np.stack([dot_rows(W_uv[h], o[h]) for h in range(W_uv.shape[0])])
+    return bf16(attn.reshape(-1))
 
 
 # ---------------------------------------------------------------------------------------------
@@ -168,11 +198,12 @@ def mla_merge_uv(partials, W_uv, step, *, split=32, d_c=None):
 
 
 def softmax_det(logits):
-    """FP32 softmax with the deterministic exp: e = det_exp(l - max l), p = e / f32(exact sum e)."""
+    """FP32 softmax with the deterministic exp: e = det_exp(l - max l), p = e / (one warp's FP32
+    sum of e: lane l adds experts l, l + 32, ..., then the butterfly)."""
     logits = np.asarray(logits, F32)
     m = logits.max(axis=-1, keepdims=True)
     e = det_exp((logits - m).astype(F32))
-    s = f32_from_f64(sum_f64(e, axis=-1))[..., None]
+    s = lane_sum(e)[..., None]
     return (e / s).astype(F32)
 
 
@@ -184,7 +215,7 @@ def moe_router(h, W_gate, *, topk=6, n_experts=64, forced=(64, 65), scaling=1.0,
     p = softmax; top-k by repeated argmax, ties to the lower index; topk_w = p * scaling, then
     1.0 per forced expert; routing [E + n_forced] (slot + 1, else 0); mask [E + n_forced + 1]
     (ids in slot order, -1 in unused entries, the count last)."""
-    logits = f32_from_f64(dot_exact(W_gate, h))
+    logits = dot_rows(W_gate, h)
     if logit_bias is not None:
         logits = (logits + np.asarray(logit_bias, F32)).astype(F32)
     p = softmax_det(logits)
@@ -243,13 +274,12 @@ def moe_w2(mid, W2, mask, n_slots=8):
 
 
 def moe_combine(out8, topk_w, x_res):
-    """x + sum_k w_k out_k in slot order, then one BF16 rounding (numpy_ref.py:316-321, the stock
-    moe_mul_sum_add). Each product (FP32 weight x BF16 value) is exact in FP64 and the FP64 sums
-    run in slot order, so the kernel's identical sequence gives identical bits."""
-    acc = np.asarray(x_res, F64).copy()
+    """x + sum_k w_k out_k in slot order, FP32 products and sums each rounded, then BF16: the
+    exact operation sequence of numpy_ref.py:316-321 (the stock moe_mul_sum_add)."""
+    acc = np.asarray(x_res, F32).copy()
     for k in range(len(topk_w)):
-        acc = acc + np.asarray(out8[k], F64) * F64(F32(topk_w[k]))
-    return bf16_from_f64(acc)
+        acc = (acc + (np.asarray(out8[k], F32) * F32(topk_w[k])).astype(F32)).astype(F32)
+    return bf16(acc)
 
 
 def dense_mlp(h, W_gu, W_down, x_res, i_dense):

@@ -35,7 +35,7 @@ def test_struct_layout():
     assert ctypes.sizeof(mk.MkOp) == 4 * 4 + 16 * 8 + 16 * 8 + 4 * 8
     assert ctypes.sizeof(mk.MkConfig) == 4 + 4 + 8 + 4 + 7 * 4
     assert ctypes.sizeof(mk.MkStatus) == 6 * 4 + 2 * 8
-    assert ctypes.sizeof(mk.MkTraceRecord) == 4 * 4 + 2 * 8
+    assert ctypes.sizeof(mk.MkTraceRecord) == 4 * 4 + 5 * 8
 
 
 def test_create_without_gpu_fails_cleanly():

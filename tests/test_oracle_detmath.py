@@ -4,6 +4,7 @@ import math
 from fractions import Fraction
 
 import numpy as np
+import pytest
 import torch
 
 from oracle import detmath as D
@@ -102,14 +103,61 @@ def test_silu_close_to_exact():
     assert np.all(np.abs(got - exact) <= 4 * np.abs(exact) * 2.0 ** -24 + 1e-37)
 
 
-def test_dot_exact_order_free():
-    """The FP64 sum of exact BF16 products rounds the same in any order (what lets a GPU
-    reduction tree and NumPy agree bit for bit)."""
-    rng = np.random.default_rng(5)
-    W = D.bf16(rng.standard_normal((64, 2048)).astype(np.float32) * 0.02)
-    x = D.bf16(rng.standard_normal(2048).astype(np.float32))
-    a = D.bf16_from_f64(D.dot_exact(W, x))
-    perm = rng.permutation(2048)
-    b = D.bf16_from_f64(D.dot_exact(W[:, perm], x[perm]))
-    c = D.bf16_from_f64(np.array([sum(float(W[i, k]) * float(x[k]) for k in range(2048)) for i in range(64)]))
-    assert np.array_equal(a, b) and np.array_equal(a, c)
+def _scalar_row_dot(w, x):
+    """The kernels' row-dot order spelled out one FP32 operation at a time."""
+    K = len(x)
+    ks, kp, maxv = D.gemv_parts(K)
+    parts = []
+    for p in range(ks):
+        lanes = []
+        for l in range(32):
+            a0, a1 = np.float32(0), np.float32(0)
+            for j in range(maxv):
+                v = l + 32 * j
+                if v * 8 >= kp:
+                    continue
+                for t in range(8):
+                    e = p * kp + 8 * v + t
+                    pr = np.float32(w[e]) * np.float32(x[e])
+                    if t % 2 == 0:
+                        a0 = np.float32(a0 + pr)
+                    else:
+                        a1 = np.float32(a1 + pr)
+            lanes.append(np.float32(a0 + a1))
+        a = np.array(lanes, np.float32)
+        for o in (16, 8, 4, 2, 1):
+            a = (a + a[np.arange(32) ^ o]).astype(np.float32)
+        parts.append(a[0])
+    d = parts[0]
+    for q in parts[1:]:
+        d = np.float32(d + q)
+    return d
+
+
+@pytest.mark.parametrize("K", [128, 384, 512, 1408, 2048, 10944])
+def test_dot_rows_is_the_specified_order(K):
+    """The vectorised emulation equals the order spelled out scalar by scalar, and stays within
+    FP32 accumulation error of the exact dot product."""
+    rng = np.random.default_rng(K)
+    W = D.bf16(rng.standard_normal((3, K)).astype(np.float32) * 0.02)
+    x = D.bf16(rng.standard_normal(K).astype(np.float32))
+    got = D.dot_rows(W, x)
+    want = np.array([_scalar_row_dot(W[i], x) for i in range(3)], np.float32)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    exact = W.astype(np.float64) @ x.astype(np.float64)
+    assert np.all(np.abs(got - exact) <= 1e-5 * np.abs(W).sum(1) * np.abs(x).max())
+
+
+def test_block_and_lane_sums():
+    rng = np.random.default_rng(6)
+    v = rng.standard_normal(2048).astype(np.float32)
+    acc = np.zeros(256, np.float32)
+    for i in range(8):
+        acc = (acc + v[i * 256:(i + 1) * 256]).astype(np.float32)
+    w = D.butterfly(acc.reshape(8, 32))
+    tot = w[0]
+    for k in range(1, 8):
+        tot = np.float32(tot + w[k])
+    assert D.block_sum(v, vec=1) == tot
+    assert abs(float(D.lane_sum(v[:70])) - float(v[:70].astype(np.float64).sum())) < 1e-5
+    assert D.seq_sum(v[:5]) == np.float32(np.float32(np.float32(np.float32(v[0] + v[1]) + v[2]) + v[3]) + v[4])
