@@ -170,6 +170,11 @@ int mk_status(MkHandle* h, MkStatus* out);
 int mk_reset(MkHandle* h);
 /* Trace records of the last launch (trace enabled): copies up to cap records, *n = count. */
 int mk_trace(MkHandle* h, MkTraceRecord* out, int64_t cap, int64_t* n);
+/* Replace the consumer-side dependencies of operator op_index (by default: the previous
+   operator) with n (1 or 2) earlier operators of the same iteration; before mk_finalize. Every
+   operator must still lead to the last one. Lets independent operators overlap (the MoE's
+   shared experts run beside the router). */
+int mk_set_op_deps(MkHandle* h, int32_t op_index, const int32_t* dep_ops, int32_t n);
 /* Schedule introspection: tasks of operator op_index, and the CTA of its task t. */
 int mk_op_tasks(MkHandle* h, int32_t op_index, int32_t* ntasks);
 /* Release everything the library allocated (replaces finalize_persistent_kernel). */
