@@ -27,8 +27,8 @@ from dataclasses import dataclass, field
 
 from fleet.pack_weights import Dims, REAL_DIMS
 
-SPLIT = 64             # latent-cache rows per attention split task
-HEAD_GROUP = 2         # query heads per attention task (8 groups x 17 splits = 136 tasks at 1,056 rows)
+SPLIT = 128            # latent-cache rows per attention split task
+HEAD_GROUP = 1         # query heads per attention task (16 heads x 9 splits = 144 tasks at 1,056 rows)
 ROUTE_LOG_ROWS = 32    # the reference's route_log [32, L - 1, 8] (fleet/graph_plan.py:376)
 RMS_EPS = 1e-6
 SOFTMAX_SCALE = 0.1147213867929261

@@ -144,7 +144,7 @@ def test_argmax_ties_to_lower_index(mk, B):
 
 @pytest.mark.parametrize("pos", [1024, 1023, 700, 64])
 def test_mla_prep_attend_merge(mk, B, pos):
-    nh, d_n, d_r, d_c, d_v, s_max, split, hg = 16, 128, 64, 512, 128, 1056, 64, 2
+    nh, d_n, d_r, d_c, d_v, s_max, split, hg = 16, 128, 64, 512, 128, 1056, 128, 1
     n_splits = -(-s_max // split)
     g = gen(pos)
     qkva = rnd_bf16(g, nh * (d_n + d_r) + d_c + d_r)

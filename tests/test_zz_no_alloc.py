@@ -34,7 +34,7 @@ def _existing(mk, B, x, pos, split, scale):
     attn = torch.zeros(nh * x["w_uv"].shape[1], dtype=torch.bfloat16, device=DEV)
     k = mk.MegaKernel(0)
     k.add(B.mla_attend_layer(mk, None, x["ql_nope"], x["q_pe"], x["c_kv"], x["k_pe"], partials, scale, split,
-                             n_splits, 2))
+                             n_splits, 1))
     k.add(B.mla_merge_uv_layer(mk, None, partials, x["w_uv"], attn, split, n_splits))
     k.finalize()
     k.launch(1, pos - 1)
