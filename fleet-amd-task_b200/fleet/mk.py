@@ -17,7 +17,7 @@ DERR = {0: "none", 1: "wait_timeout", 2: "ring_timeout", 3: "token_range", 4: "a
 
 # operator types and flags
 OP_EMBED, OP_GEMV, OP_MLA_PREP, OP_MLA_ATTEND, OP_MLA_MERGE_UV, OP_ROUTER, OP_GATEUP, OP_W2_COMBINE, OP_STREAM = range(1, 10)
-F_NORM, F_RESIDUAL, F_ARGMAX, F_EXPERT = 1, 2, 4, 8
+F_NORM, F_RESIDUAL, F_ARGMAX, F_EXPERT, F_STATIC_IDS = 1, 2, 4, 8, 16
 
 # ptr / ip indices (mirrors the enums of fleet_mk.h)
 P = dict(

@@ -71,6 +71,7 @@ enum MkOpType {
 #define MK_F_RESIDUAL (1 << 1)   /* GEMV: add res before the rounding */
 #define MK_F_ARGMAX (1 << 2)     /* GEMV: greedy argmax of the output into tokens[pos + 1] */
 #define MK_F_EXPERT (1 << 3)     /* GATEUP: groups are the routed slots of `mask` */
+#define MK_F_STATIC_IDS (1 << 4) /* GATEUP: `mask` holds constant expert ids (no wait for a router) */
 
 #define MK_MAX_PTRS 16
 #define MK_MAX_IPARAMS 16

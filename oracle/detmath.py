@@ -124,8 +124,10 @@ def from_bf16_bits(b):
 
 
 def gemv_parts(K):
-    """(KS, kp, MAXV) of a row of K values, as the kernels choose them."""
-    ks = 1 if K <= 1024 else (2 if K <= 2048 else 8)
+    """(KS, kp, MAXV) of a row of K values, as the kernels choose them: for K <= 2048 the fewest of
+    1, 2, 4 or 8 equal parts of at most 256 values (one 8-value vector per lane, MAXV 1); wider
+    rows (the dense down projection) 8 parts of K / 8 values, MAXV vectors per lane."""
+    ks = next(k for k in (1, 2, 4, 8) if K <= 256 * k) if K <= 2048 else 8
     assert K % (8 * ks) == 0, (K, ks)
     kp = K // ks
     return ks, kp, -(-kp // 256)

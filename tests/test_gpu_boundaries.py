@@ -42,7 +42,8 @@ CHECKS = {   # label suffix -> [(workspace, record key, slice)]
     "gate_up": [("act0", "act", None), ("h", "norm2", None)],
     "down": [("x_res", "layer_out", None)],
     "router": [("h", "norm2", None)],
-    "w13": [("act8", None, None)],
+    "w13s": [("act8", None, None)],
+    "w13r": [("act8", None, None)],
     "w2_combine": [("x_res", "layer_out", None), ("out8", "out8", None)],
 }
 
@@ -88,10 +89,11 @@ def test_every_boundary(which, split):
                 if not np.array_equal(got[:live].view(np.uint32), want[:live].view(np.uint32)):
                     bad = np.nonzero(got[:live] != want[:live])
                     failures.append(f"{lab}: partials differ at {len(bad[0])} places, first {tuple(b[0] for b in bad)}")
-            if op == "w13":
+            if op in ("w13s", "w13r"):   # shared slots TOPK.. / routed slots ..TOPK of act8
                 mask = rec[f"{prefix}.mask"]
                 act = np.stack([R.swiglu_act(m, dims.I_MOE) for m in rec[f"{prefix}.mid"][:int(mask[-1])]])
-                if not np.array_equal(np32(host["act8"])[:len(act)], act):
+                rows = slice(dims.TOPK, dims.TOPK + dims.N_SHARED) if op == "w13s" else slice(0, dims.TOPK)
+                if not np.array_equal(np32(host["act8"])[rows], act[rows]):
                     failures.append(f"{lab}: act8")
                 checks = []
         for ws, key in checks:

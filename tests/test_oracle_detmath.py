@@ -148,6 +148,16 @@ def test_dot_rows_is_the_specified_order(K):
     assert np.all(np.abs(got - exact) <= 1e-5 * np.abs(W).sum(1) * np.abs(x).max())
 
 
+def test_gemv_partition():
+    assert D.gemv_parts(2048) == (8, 256, 1)
+    assert D.gemv_parts(1408) == (8, 176, 1)
+    assert D.gemv_parts(1024) == (4, 256, 1)
+    assert D.gemv_parts(512) == (2, 256, 1)
+    assert D.gemv_parts(384) == (2, 192, 1)
+    assert D.gemv_parts(128) == (1, 128, 1)
+    assert D.gemv_parts(10944) == (8, 1368, 6)
+
+
 def test_block_and_lane_sums():
     rng = np.random.default_rng(6)
     v = rng.standard_normal(2048).astype(np.float32)
