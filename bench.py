@@ -68,18 +68,46 @@ def dist_env():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region: NVML polled every 2 ms from
+    a thread (a 16-token region lasts ~50 ms, shorter than nvidia-smi's start-up), else nvidia-smi
+    every 200 ms. Read-only: no clock or setting is changed."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"sw_power_cap": "SwPowerCap", "hw_slowdown": "HwSlowdown", "sw_thermal_slowdown": "SwThermalSlowdown",
+               "hw_thermal_slowdown": "HwThermalSlowdown"}
 
-    def __init__(self, index):
+    def __init__(self, index, torch_device=None):
         self.index = index
+        self.torch_device = torch_device
         self.proc = None
         self.lines = []
+        self.samples = []         # (sm_mhz, reason bits) from NVML
+        self.max_mhz = None
+        self.nvml = None
+        self._stop = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            pr = torch.cuda.get_device_properties(self.torch_device if self.torch_device is not None else 0)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def __enter__(self):
+        try:
+            self.nvml, self.h = self._nvml_handle()
+            self.max_mhz = float(self.nvml.nvmlDeviceGetMaxClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -90,11 +118,26 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _poll(self):
+        nv = self.nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        while not self._stop.is_set():
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)),
+                                     int(get_reasons(self.h))))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        self._stop.set()
+        if self.nvml is not None:
+            self.t.join(timeout=2)
         if self.proc:
             self.proc.terminate()
             try:
@@ -104,6 +147,13 @@ class ClockSampler:
             self.t.join(timeout=2)
 
     def summary(self):
+        if self.nvml is not None:
+            sm = [c for c, _ in self.samples]
+            bits_of = {nm: getattr(self.nvml, f"nvmlClocksEventReason{k}", None) or
+                       getattr(self.nvml, f"nvmlClocksThrottleReason{k}") for nm, k in self.REASONS.items()}
+            reasons = sorted({nm for _, bits in self.samples for nm, b in bits_of.items() if bits & b})
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(sm), "source": "nvml"}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.lines:
@@ -119,7 +169,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -294,7 +344,7 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     ctx0 = mpk.step + 2
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, local) as clk:
         per = time_steps(mpk, meta, args.steps, torch, stream)
     torch.cuda.synchronize()
     if dist:
