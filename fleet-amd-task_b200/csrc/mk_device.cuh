@@ -132,12 +132,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // global -> shared bulk copy (no tensor map); completes `bytes` of transaction on `bar`.
-// Requirements: 16-byte aligned addresses, bytes a multiple of 16.
+// Requirements: 16-byte aligned addresses, bytes a multiple of 16. The copy carries an L2
+// evict-first policy: weights stream through L2 once per token, and without the hint they push
+// the kernel's instructions, activations and split-KV partials out of L2.
 __device__ __forceinline__ void bulk_g2s(void* sdst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
           smem_u32(sdst)),
-      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 // explicit shared-memory loads (the address is a shared-window offset, smem_u32)
