@@ -89,12 +89,13 @@ __device__ bool produce_task(const KernelParams& P, Smem& sm, Prod& pr, const Op
       const int32_t* mask = P_<const int32_t>(od, MK_P_GU_MASK);
       const int64_t estride = I_(od, MK_I_GU_ESTRIDE);
       const int nexp = (int)I_(od, MK_I_GU_NEXP);
-      int p = t.a;
+      const GuMap gm = gu_map(od, t);
+      int p = gm.a;
       GuChunk ch;
-      while (gu_next(od, p, t.b, ch)) {
+      while (gu_next(od, p, gm.b, ch)) {
         int e = 0;
         if (expert) {
-          e = __ldcg(mask + ch.group);
+          e = __ldcg(mask + gm.slot[ch.group]);
           if (e < 0 || e >= nexp) { report_error(P, sm, MK_DERR_BAD_EXPERT, op, task, (uint32_t)e); return false; }
         }
         const uint8_t* src = W + ((size_t)e * (size_t)estride + (size_t)ch.q * 2 * K) * 2;
@@ -110,8 +111,10 @@ __device__ bool produce_task(const KernelParams& P, Smem& sm, Prod& pr, const Op
       const int64_t estride = I_(od, MK_I_W2_ESTRIDE);
       const int nexp = (int)I_(od, MK_I_W2_NEXP);
       (void)H;
-      for (int s = 0; s < NS; ++s) {
-        const int e = __ldcg(mask + s);
+      (void)NS;
+      const W2Slots ws = w2_slots(od);
+      for (int k = 0; k < ws.n; ++k) {
+        const int e = __ldcg(mask + ws.slot[k]);
         if (e < 0 || e >= nexp) { report_error(P, sm, MK_DERR_BAD_EXPERT, op, task, (uint32_t)e); return false; }
         const uint8_t* base = W + (size_t)e * (size_t)estride * 2;
         for (int r = t.a; r < t.b; r += od.rps) {
@@ -884,11 +887,12 @@ __device__ void gateup_body(const KernelParams& P, Smem& sm, const OpDev& od, co
   (void)itx;
   mark_body(sm, c);
   float* pbuf = pbuf_of(sm);   // [2 * pairs][KS]: local row 2 lp = gate, 2 lp + 1 = up
-  int p = t.a;
+  const GuMap gm = gu_map(od, t);
+  int p = gm.a;
   GuChunk ch;
-  while (gu_next(od, p, t.b, ch)) {
+  while (gu_next(od, p, gm.b, ch)) {
     const uint8_t* stg = acquire_stage(P, sm, c, (uint32_t)t.op, (uint32_t)t.idx);
-    const int base = (ch.group * I + ch.q) - t.a;   // local pair index of the chunk's first pair
+    const int base = (ch.group * I + ch.q) - gm.a;   // local pair index of the chunk's first pair
     stage_parts<KS>(stg, 2 * ch.np, K, 2 * base, pbuf, c, [&](int) { return xv; });
     release_stage(sm, c);
   }
@@ -896,8 +900,8 @@ __device__ void gateup_body(const KernelParams& P, Smem& sm, const OpDev& od, co
   consumer_sync();
   uint16_t* act = P_<uint16_t>(od, MK_P_GU_ACT);
   uint16_t* mid = P_<uint16_t>(od, MK_P_GU_MID);
-  for (int lp = c.tid; lp < t.b - t.a; lp += NUM_CONSUMERS) {
-    const int gp = t.a + lp, g = gp / I, q = gp % I;
+  for (int lp = c.tid; lp < gm.b - gm.a; lp += NUM_CONSUMERS) {
+    const int gp = gm.a + lp, g = gm.slot[gp / I], q = gp % I;
     const uint32_t gb = f32_to_bf16_bits(row_total<KS>(pbuf, 2 * lp));
     const uint32_t ub = f32_to_bf16_bits(row_total<KS>(pbuf, 2 * lp + 1));
     const float a = __fmul_rn(det_silu(bf16_bits_to_f32(gb)), bf16_bits_to_f32(ub));
@@ -907,12 +911,16 @@ __device__ void gateup_body(const KernelParams& P, Smem& sm, const OpDev& od, co
 }
 
 // ---- expert down projection per slot, then the weighted combine into x_res ------------------
+// With MK_F_EP the task computes its rank's slots (w2_slots), writes their out8 rows, stores the
+// routed ones into every peer's out8 too and signals the peers' counters; MK_OP_EP_COMBINE adds.
 template <int KS>
 __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const TaskDev& t, const Iter& itx,
                         Cons& c) {
   const int H = (int)I_(od, MK_I_W2_H), I = (int)I_(od, MK_I_W2_I), NS = (int)I_(od, MK_I_W2_SLOTS);
   const uint16_t* act = P_<const uint16_t>(od, MK_P_W2_ACT);
   const int nr_t = t.b - t.a;
+  const bool ep = (od.op.flags & MK_F_EP) != 0;
+  const W2Slots ws = w2_slots(od);
   // all slots' activations staged in shared memory with one round of 16-byte loads
   uint16_t* abuf = reinterpret_cast<uint16_t*>(sm.scratch);                         // NS x I
   float* pbuf = reinterpret_cast<float*>(sm.scratch + W2_PBUF_OFF);                  // [NS * rows][KS]
@@ -921,7 +929,8 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
   consumer_sync();
   mark_body(sm, c);
   (void)itx;
-  for (int s = 0; s < NS; ++s) {
+  for (int k = 0; k < ws.n; ++k) {
+    const int s = ws.slot[k];
     const uint4 xv = x_part<KS, true>(abuf + (size_t)s * I, I, c);
     for (int r0 = t.a; r0 < t.b; r0 += od.rps) {
       const int nr = min(od.rps, t.b - r0);
@@ -932,9 +941,32 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
   }
   mark_stages(sm, c);
   consumer_sync();
+  uint16_t* out8 = P_<uint16_t>(od, MK_P_W2_OUT8);
+  if (ep) {
+    const MkEpPeers* pe = P_<const MkEpPeers>(od, MK_P_W2_PEERS);
+    const int TOPK = (int)I_(od, MK_I_W2_TOPK), nranks = pe->nranks, me = pe->rank;
+    // the exchange buffers alternate by layer parity: a peer writes layer l + 2's rows only after
+    // this rank's layer l + 1 rows reached it, which follows this rank's layer l combine
+    const size_t half = ((size_t)I_(od, MK_I_W2_LAYER) & 1u) * (size_t)NS * H;
+    for (int i = c.tid; i < ws.n * nr_t; i += NUM_CONSUMERS) {
+      const int k = i / nr_t, lr = i - k * nr_t, s = ws.slot[k], row = t.a + lr;
+      const uint16_t ob = (uint16_t)f32_to_bf16_bits(row_total<KS>(pbuf, s * nr_t + lr));
+      out8[half + (size_t)s * H + row] = ob;
+      if (s < TOPK)
+        for (int r = 0; r < nranks; ++r)
+          if (r != me) reinterpret_cast<uint16_t*>(pe->out8[r])[half + (size_t)s * H + row] = ob;
+    }
+    consumer_sync();
+    if (c.tid == 0) {   // the stores above happen before the peers see the count (system scope)
+      __threadfence_system();
+      const int layer = (int)I_(od, MK_I_W2_LAYER);
+      for (int r = 0; r < nranks; ++r)
+        if (r != me) red_release_sys_add(pe->counter[r] + layer, 1u);
+    }
+    return;
+  }
   const float* topk_w = P_<const float>(od, MK_P_W2_TOPKW);
   uint16_t* xres = P_<uint16_t>(od, MK_P_W2_XRES);
-  uint16_t* out8 = P_<uint16_t>(od, MK_P_W2_OUT8);
   for (int lr = c.tid; lr < nr_t; lr += NUM_CONSUMERS) {
     const int row = t.a + lr;
     float acc = bf16_bits_to_f32(ldcg_u16(xres + row));
@@ -945,6 +977,41 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
     }
     xres[row] = (uint16_t)f32_to_bf16_bits(acc);
   }
+}
+
+// ---- expert-parallel combine: wait for the peers' out8 rows, then the slot-order sum ---------
+__device__ void ep_combine_body(const KernelParams& P, Smem& sm, const OpDev& od, const TaskDev& t, const Iter& itx,
+                                Cons& c) {
+  const int H = (int)I_(od, MK_I_EC_H), NS = (int)I_(od, MK_I_EC_SLOTS), layer = (int)I_(od, MK_I_EC_LAYER);
+  const MkEpPeers* pe = P_<const MkEpPeers>(od, MK_P_EC_PEERS);
+  if (c.tid == 0) {
+    // every peer's w2 tasks add 1 per iteration (bounded wait, system scope)
+    const uint32_t target = (uint32_t)(pe->nranks - 1) * (uint32_t)I_(od, MK_I_EC_W2TASKS) * itx.g;
+    const uint32_t* ctr = pe->counter[pe->rank] + layer;
+    const uint64_t t0 = globaltimer();
+    int ok = 1;
+    for (uint32_t n = 0;; ++n) {
+      if ((int32_t)(ld_acquire_sys_u32(ctr) - target) >= 0) break;
+      if ((n & 31u) == 31u && (aborted(P, sm) || (int64_t)(globaltimer() - t0) > P.timeout_ns)) { ok = 0; break; }
+    }
+    if (!ok)
+      report_error(P, sm, *(volatile uint32_t*)&P.status->abort_flag ? MK_DERR_ABORTED : MK_DERR_WAIT_TIMEOUT,
+                   (uint32_t)t.op, (uint32_t)t.idx, 0x20000u | (uint32_t)layer);
+    sm.bcast[2] = ok;
+  }
+  consumer_sync();
+  mark_body(sm, c);
+  if (!sm.bcast[2]) return;
+  const uint16_t* out8 = P_<const uint16_t>(od, MK_P_EC_OUT8) + ((size_t)layer & 1u) * (size_t)NS * H;
+  const float* topk_w = P_<const float>(od, MK_P_EC_TOPKW);
+  uint16_t* xres = P_<uint16_t>(od, MK_P_EC_XRES);
+  for (int row = t.a + c.tid; row < t.b; row += NUM_CONSUMERS) {
+    float acc = bf16_bits_to_f32(ldcg_u16(xres + row));
+    for (int s = 0; s < NS; ++s)   // numpy_ref.moe_combine's operation order: acc + f32(out * w)
+      acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(ldcg_u16(out8 + (size_t)s * H + row)), ldcg_f32(topk_w + s)));
+    xres[row] = (uint16_t)f32_to_bf16_bits(acc);
+  }
+  mark_stages(sm, c);
 }
 
 // ---- stream probe: the ring's bytes, no arithmetic -------------------------------------------
@@ -1012,6 +1079,7 @@ __device__ void run_task(const KernelParams& P, Smem& sm, const OpDev& od, const
       by_parts(I, [&](auto ks) { w2_body<decltype(ks)::value>(P, sm, od, t, itx, c); });
       break;
     }
+    case MK_OP_EP_COMBINE: ep_combine_body(P, sm, od, t, itx, c); break;
     case MK_OP_STREAM: op_stream(P, sm, od, t, itx, c); break;
     default: break;
   }

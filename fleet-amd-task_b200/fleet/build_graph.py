@@ -76,27 +76,47 @@ def moe_router_layer(mk, t, input, w_norm, w_gate, h, topk_w, routing, mask, log
 
 
 def gateup_layer(mk, t, input, weight, act, inter, groups, expert, norm, w_norm=None, mask=None, mid=None, h_out=None,
-                 eps=G.RMS_EPS, static_ids=False):
+                 eps=G.RMS_EPS, static_ids=False, ep_range=None):
     """static_ids: the mask holds constant expert ids (the shared experts), so the weights stream
-    without waiting for a router."""
+    without waiting for a router. ep_range (lo, hi): expert parallelism, only the slots whose
+    expert is in [lo, hi), spread over the tasks at run time."""
     K = weight.shape[-1]
     estride = weight.shape[-2] * K if weight.dim() == 3 else 0
     nexp = weight.shape[0] if weight.dim() == 3 else 1
     flags = (mk.F_EXPERT if expert else 0) | (mk.F_NORM if norm else 0) | (mk.F_STATIC_IDS if static_ids else 0)
+    ips = {0: K, 1: inter, 2: groups, 3: estride, 4: nexp}
+    if ep_range is not None:
+        flags |= mk.F_EP
+        ips.update({5: ep_range[0], 6: ep_range[1]})
     u = mk.P["gu"]
     return mk.make_op(mk.OP_GATEUP, flags, {u["X"]: input, u["WNORM"]: w_norm, u["W"]: weight, u["MASK"]: mask,
-                                            u["MID"]: mid, u["ACT"]: act, u["HOUT"]: h_out},
-                      {0: K, 1: inter, 2: groups, 3: estride, 4: nexp}, {0: eps})
+                                            u["MID"]: mid, u["ACT"]: act, u["HOUT"]: h_out}, ips, {0: eps})
 
 
-def moe_w2_combine_layer(mk, t, input, weight, mask, topk_w, residual, output, out8=None):
+def moe_w2_combine_layer(mk, t, input, weight, mask, topk_w, residual, output, out8=None, ep_range=None, peers=None,
+                         topk=None, layer=0):
+    """ep_range (lo, hi): expert parallelism; the task writes its rank's slots' out8 rows (the
+    routed ones into every peer's out8 too, through `peers`) and ep_combine_layer adds them."""
     E, H, I = weight.shape
     assert residual.data_ptr() == output.data_ptr(), "the combine adds into x_res in place"
     n_slots = input.shape[0]
     w = mk.P["w2"]
-    return mk.make_op(mk.OP_W2_COMBINE, 0, {w["ACT"]: input, w["W"]: weight, w["MASK"]: mask, w["TOPKW"]: topk_w,
-                                            w["XRES"]: output, w["OUT8"]: out8},
-                      {0: H, 1: I, 2: n_slots, 3: H * I, 4: E})
+    flags, ips = 0, {0: H, 1: I, 2: n_slots, 3: H * I, 4: E}
+    if ep_range is not None:
+        flags = mk.F_EP
+        ips.update({5: topk, 6: ep_range[0], 7: ep_range[1], 8: layer})
+    return mk.make_op(mk.OP_W2_COMBINE, flags, {w["ACT"]: input, w["W"]: weight, w["MASK"]: mask, w["TOPKW"]: topk_w,
+                                                w["XRES"]: output, w["OUT8"]: out8, w["PEERS"]: peers}, ips)
+
+
+def ep_combine_layer(mk, t, out8, topk_w, residual, output, peers, layer, w2_tasks):
+    """Expert parallelism: wait for every peer's out8 rows of `layer`, then x_res += sum w out8 in
+    slot order (numpy_ref.moe_combine)."""
+    assert residual.data_ptr() == output.data_ptr(), "the combine adds into x_res in place"
+    _, n_slots, H = out8.shape
+    c = mk.P["ec"]
+    return mk.make_op(mk.OP_EP_COMBINE, 0, {c["OUT8"]: out8, c["TOPKW"]: topk_w, c["XRES"]: output, c["PEERS"]: peers},
+                      {0: H, 1: n_slots, 2: layer, 3: w2_tasks})
 
 
 def stream_layer(mk, t, weight, dummy, dummy_in=None):
@@ -107,7 +127,7 @@ NEW_LAYERS = {
     "embed_layer": embed_layer, "linear_gemv_layer": linear_gemv_layer, "mla_prep_layer": mla_prep_layer,
     "mla_attend_layer": mla_attend_layer, "mla_merge_uv_layer": mla_merge_uv_layer,
     "moe_router_layer": moe_router_layer, "gateup_layer": gateup_layer,
-    "moe_w2_combine_layer": moe_w2_combine_layer, "stream_layer": stream_layer,
+    "moe_w2_combine_layer": moe_w2_combine_layer, "stream_layer": stream_layer, "ep_combine_layer": ep_combine_layer,
 }
 
 
@@ -239,14 +259,20 @@ class MPK:
 
 def build(packed, capture, meta, dims=REAL_DIMS, s_max=1056, layers=27, head=True, debug=False, stop_after=None,
           split=G.SPLIT, head_group=G.HEAD_GROUP, num_ctas=0, device=None, trace=False, wait_timeout_s=2.0,
-          plan=None, workspaces=None, logit_bias=False):
+          plan=None, workspaces=None, logit_bias=False, ep=None):
     """On the machine: the plan, its tensors, one library operator per call -> (mpk, host, plan).
-    plan: a ready plan (the stream probe) instead of the model's."""
+    plan: a ready plan (the stream probe) instead of the model's. ep: an fleet.ep.EpGroup (expert
+    parallelism; every rank calls build with the same arguments and its own group)."""
     import torch
     from fleet import mk
 
     if plan is None:
-        plan = G.build_plan(dims, s_max, layers, head, debug, split, head_group, logit_bias=logit_bias)
+        plan = G.build_plan(dims, s_max, layers, head, debug, split, head_group, logit_bias=logit_bias,
+                            ep=None if ep is None else (ep.rank, ep.world))
+    if ep is not None:
+        workspaces = dict(workspaces or {})
+        workspaces["ep_out8"] = ep.out8
+        workspaces["ep_peers"] = ep.peers
     if stop_after:
         plan.truncate(stop_after)
     assert not plan.chain_violations(), f"the chain is broken: {plan.chain_violations()}"
@@ -256,7 +282,10 @@ def build(packed, capture, meta, dims=REAL_DIMS, s_max=1056, layers=27, head=Tru
     n_cta = num_ctas or torch.cuda.get_device_properties(dev).multi_processor_count
     index = {}
     for i, c in enumerate(plan.calls):
-        op = NEW_LAYERS[c.method](mk, None, **call_kwargs(c, host))
+        kw = call_kwargs(c, host)
+        if c.method == "ep_combine_layer":       # the combine counts the down projection's tasks
+            kw["w2_tasks"] = kernel.tasks(index[kw.pop("w2_label")])
+        op = NEW_LAYERS[c.method](mk, None, **kw)
         if c.beside and op.ntasks == 0:
             # the operators it runs beside keep their CTAs; it takes the rest (tasks are dealt to
             # CTAs in chain order from a rotating start, so the free CTAs are the next ones)
@@ -304,8 +333,9 @@ class FakeTensor:
 
 class FakeMk:
     """Records operators instead of calling the library (the reference's FakeMPK role)."""
-    OP_EMBED, OP_GEMV, OP_MLA_PREP, OP_MLA_ATTEND, OP_MLA_MERGE_UV, OP_ROUTER, OP_GATEUP, OP_W2_COMBINE, OP_STREAM = range(1, 10)
-    F_NORM, F_RESIDUAL, F_ARGMAX, F_EXPERT, F_STATIC_IDS = 1, 2, 4, 8, 16
+    (OP_EMBED, OP_GEMV, OP_MLA_PREP, OP_MLA_ATTEND, OP_MLA_MERGE_UV, OP_ROUTER, OP_GATEUP, OP_W2_COMBINE, OP_STREAM,
+     OP_EP_COMBINE) = range(1, 11)
+    F_NORM, F_RESIDUAL, F_ARGMAX, F_EXPERT, F_STATIC_IDS, F_EP = 1, 2, 4, 8, 16, 32
 
     def __init__(self):
         from fleet.mk import P
@@ -325,16 +355,21 @@ class FakeMk:
 
 
 def dry_run(dims=REAL_DIMS, s_max=1056, layers=27, head=True, debug=False, stop_after=None, split=G.SPLIT,
-            head_group=G.HEAD_GROUP):
-    """The plan and every operator's parameters, without a GPU: returns (plan, recorded ops)."""
-    plan = G.build_plan(dims, s_max, layers, head, debug, split, head_group)
+            head_group=G.HEAD_GROUP, ep=None):
+    """The plan and every operator's parameters, without a GPU: returns (plan, recorded ops).
+    ep (rank, world): the expert-parallel plan of that rank."""
+    plan = G.build_plan(dims, s_max, layers, head, debug, split, head_group, ep=ep)
     if stop_after:
         plan.truncate(stop_after)
     assert not plan.chain_violations(), plan.chain_violations()
     host = {n: FakeTensor(n, t.shape, t.dtype) for n, t in plan.tensors.items()}
     fmk = FakeMk()
     for c in plan.calls:
-        NEW_LAYERS[c.method](fmk, None, **call_kwargs(c, host))
+        kw = call_kwargs(c, host)
+        if c.method == "ep_combine_layer":
+            kw.pop("w2_label")
+            kw["w2_tasks"] = 1
+        NEW_LAYERS[c.method](fmk, None, **kw)
     set_plan_deps(plan, fmk)
     return plan, fmk.ops
 

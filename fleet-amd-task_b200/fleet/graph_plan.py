@@ -43,6 +43,16 @@ def float_bits(x: float) -> int:
     return struct.unpack("<i", struct.pack("<f", x))[0]
 
 
+EP_PEERS_WORDS = 36          # sizeof(MkEpPeers) / 4
+
+
+def ep_expert_range(rank, world, n_experts):
+    """The routed experts rank `rank` of `world` owns under expert parallelism: [lo, hi)."""
+    assert n_experts % world == 0 and 0 <= rank < world, (n_experts, rank, world)
+    per = n_experts // world
+    return rank * per, (rank + 1) * per
+
+
 def partials_row(d_c):
     """Innermost width of the split-KV partials: D_C values of o, the lse at column D_C, padded to a
     multiple of 4 floats so every [split, head] row is 16-byte aligned (513 -> 516 at D_C 512)."""
@@ -95,6 +105,7 @@ OUTPUT_ARGS = {
     "moe_router_layer": ["h", "topk_w", "routing", "mask", "logits", "route_log"],
     "gateup_layer": ["act", "mid", "h_out"],
     "moe_w2_combine_layer": ["output", "out8"],
+    "ep_combine_layer": ["output"],
     "stream_layer": ["dummy"],
 }
 
@@ -175,10 +186,13 @@ class Plan:
 
 def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head: bool = True,
                debug: bool = False, split: int = SPLIT, head_group: int = HEAD_GROUP,
-               route_log_rows: int = ROUTE_LOG_ROWS, logit_bias: bool = False, softmax_scale: float = None) -> Plan:
+               route_log_rows: int = ROUTE_LOG_ROWS, logit_bias: bool = False, softmax_scale: float = None,
+               ep: tuple = None) -> Plan:
     """The operator chain for `layers` layers (+ the head). logit_bias: every router adds an
     injected FP32 bias [E] to its logits (the skewed/uniform routing of config 3). softmax_scale:
-    default q_head_dim^-0.5 times the YaRN mscale^2 of the dims (0.1147213867929261 at REAL_DIMS)."""
+    default q_head_dim^-0.5 times the YaRN mscale^2 of the dims (0.1147213867929261 at REAL_DIMS).
+    ep (rank, world): expert parallelism (fleet/ep.py): this rank's routed gate/up and down
+    projection cover its own experts, and an ep_combine waits for the peers' rows."""
     from fleet.capture import softmax_scale as yarn_softmax_scale
     d = dims
     scale = yarn_softmax_scale(d.D_N, d.D_R) if softmax_scale is None else softmax_scale
@@ -211,6 +225,9 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
         p.t("act8", (d.N_SLOTS, d.I_MOE))
         p.t("out8", (d.N_SLOTS, d.H))
         p.t("route_log", (route_log_rows, d.L - 1, d.N_SLOTS), "i32")
+        if ep is not None:
+            p.t("ep_out8", (2, d.N_SLOTS, d.H))
+            p.t("ep_peers", (EP_PEERS_WORDS,), "i32")
     p.op("embed_layer", "prologue.embed", input="tokens", weight="W_embed", output="x_res")
     for l in range(layers):
         p.t(f"w_norm1_{l}", (d.H,), kind="input", source=f"w_norm1_{l}")
@@ -258,10 +275,21 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
                  w_norm=f"w_norm2_{l}",
                  weight=f"W13_{l}", mask="mask_shared", mid=Rows("mid", d.TOPK), act=Rows("act8", d.TOPK),
                  groups=d.N_SHARED, expert=True, static_ids=True, norm=True, eps=RMS_EPS, inter=d.I_MOE)
-            p.op("gateup_layer", f"L{l}.w13r", deps=(f"L{l}.router",), input="h", weight=f"W13_{l}", mask="mask",
-                 mid="mid", act="act8", groups=d.TOPK, expert=True, norm=False, inter=d.I_MOE)
-            p.op("moe_w2_combine_layer", f"L{l}.w2_combine", deps=(f"L{l}.w13r", f"L{l}.w13s"), input="act8",
-                 weight=f"W2_{l}", mask="mask", topk_w="topk_w", residual="x_res", output="x_res", out8="out8")
+            if ep is None:
+                p.op("gateup_layer", f"L{l}.w13r", deps=(f"L{l}.router",), input="h", weight=f"W13_{l}",
+                     mask="mask", mid="mid", act="act8", groups=d.TOPK, expert=True, norm=False, inter=d.I_MOE)
+                p.op("moe_w2_combine_layer", f"L{l}.w2_combine", deps=(f"L{l}.w13r", f"L{l}.w13s"), input="act8",
+                     weight=f"W2_{l}", mask="mask", topk_w="topk_w", residual="x_res", output="x_res", out8="out8")
+            else:
+                rng = ep_expert_range(ep[0], ep[1], d.E)
+                p.op("gateup_layer", f"L{l}.w13r", deps=(f"L{l}.router",), input="h", weight=f"W13_{l}",
+                     mask="mask", mid="mid", act="act8", groups=d.TOPK, expert=True, norm=False, inter=d.I_MOE,
+                     ep_range=rng)
+                p.op("moe_w2_combine_layer", f"L{l}.w2_combine", deps=(f"L{l}.w13r", f"L{l}.w13s"), input="act8",
+                     weight=f"W2_{l}", mask="mask", topk_w="topk_w", residual="x_res", output="x_res",
+                     out8="ep_out8", ep_range=rng, peers="ep_peers", topk=d.TOPK, layer=l - 1)
+                p.op("ep_combine_layer", f"L{l}.ep_combine", out8="ep_out8", topk_w="topk_w", residual="x_res",
+                     output="x_res", peers="ep_peers", layer=l - 1, w2_label=f"L{l}.w2_combine")
     if head:
         p.t("w_final_norm", (d.H,), kind="input", source="w_final_norm")
         p.t("W_lm", (d.V, d.H), kind="input", source="W_lm")

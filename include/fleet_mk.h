@@ -63,7 +63,10 @@ enum MkOpType {
                              layer 0's gang_linear_silu) */
   MK_OP_W2_COMBINE = 8,   /* out8 = W2 act per slot, x += sum w out8     (gang_moe_w2_silu_mi300.cuh
                              + moe_mul_sum_add) */
-  MK_OP_STREAM = 9        /* read-only bandwidth probe of the weight ring (stream_mi300.cuh:99) */
+  MK_OP_STREAM = 9,       /* read-only bandwidth probe of the weight ring (stream_mi300.cuh:99) */
+  MK_OP_EP_COMBINE = 10   /* expert parallelism: wait until every peer rank has stored its routed
+                             slots' out8 rows here, then x += sum w out8 in slot order (the
+                             exchange + moe_mul_sum_add of the expert-parallel configurations) */
 };
 
 /* MkOp.flags */
@@ -72,6 +75,12 @@ enum MkOpType {
 #define MK_F_ARGMAX (1 << 2)     /* GEMV: greedy argmax of the output into tokens[pos + 1] */
 #define MK_F_EXPERT (1 << 3)     /* GATEUP: groups are the routed slots of `mask` */
 #define MK_F_STATIC_IDS (1 << 4) /* GATEUP: `mask` holds constant expert ids (no wait for a router) */
+#define MK_F_EP (1 << 5)         /* GATEUP / W2_COMBINE: expert parallelism. GATEUP computes only the
+                                    routed slots whose expert is in [ep_lo, ep_hi), spread over its
+                                    tasks at run time; W2_COMBINE computes those slots and the shared
+                                    ones, stores the routed slots' out8 rows into every peer's out8
+                                    and signals the peers' counters, and leaves the combine to
+                                    MK_OP_EP_COMBINE */
 
 #define MK_MAX_PTRS 16
 #define MK_MAX_IPARAMS 16
@@ -111,10 +120,26 @@ enum { /* MK_OP_ROUTER */ MK_P_RT_X = 0, MK_P_RT_WNORM = 1, MK_P_RT_WGATE = 2, M
        MK_I_RT_LOGSTRIDE = 5, MK_I_RT_LOGROWS = 6 };
 enum { /* MK_OP_GATEUP */ MK_P_GU_X = 0, MK_P_GU_WNORM = 1, MK_P_GU_W = 2, MK_P_GU_MASK = 3,
        MK_P_GU_MID = 4, MK_P_GU_ACT = 5, MK_P_GU_HOUT = 6,
-       MK_I_GU_K = 0, MK_I_GU_I = 1, MK_I_GU_GROUPS = 2, MK_I_GU_ESTRIDE = 3, MK_I_GU_NEXP = 4 };
+       MK_I_GU_K = 0, MK_I_GU_I = 1, MK_I_GU_GROUPS = 2, MK_I_GU_ESTRIDE = 3, MK_I_GU_NEXP = 4,
+       MK_I_GU_EPLO = 5, MK_I_GU_EPHI = 6 };
 enum { /* MK_OP_W2_COMBINE */ MK_P_W2_ACT = 0, MK_P_W2_W = 1, MK_P_W2_MASK = 2, MK_P_W2_TOPKW = 3,
        MK_P_W2_XRES = 4, MK_P_W2_OUT8 = 5,
-       MK_I_W2_H = 0, MK_I_W2_I = 1, MK_I_W2_SLOTS = 2, MK_I_W2_ESTRIDE = 3, MK_I_W2_NEXP = 4 };
+       MK_P_W2_PEERS = 6,   /* MK_F_EP: device MkEpPeers */
+       MK_I_W2_H = 0, MK_I_W2_I = 1, MK_I_W2_SLOTS = 2, MK_I_W2_ESTRIDE = 3, MK_I_W2_NEXP = 4,
+       MK_I_W2_TOPK = 5, MK_I_W2_EPLO = 6, MK_I_W2_EPHI = 7, MK_I_W2_LAYER = 8 };
+enum { /* MK_OP_EP_COMBINE */ MK_P_EC_OUT8 = 0, MK_P_EC_TOPKW = 1, MK_P_EC_XRES = 2, MK_P_EC_PEERS = 3,
+       MK_I_EC_H = 0, MK_I_EC_SLOTS = 1, MK_I_EC_LAYER = 2, MK_I_EC_W2TASKS = 3 };
+
+/* Expert parallelism: where each rank's exchange buffers are, as this rank maps them (peer
+   pointers opened with mk_ep_ipc_open). out8[r] is rank r's [slots, H] BF16 out8 buffer and
+   counter[r] its array of per-MoE-layer arrival counters (32-bit, monotonic). */
+#define MK_EP_MAX_RANKS 8
+typedef struct MkEpPeers {
+  void* out8[MK_EP_MAX_RANKS];
+  uint32_t* counter[MK_EP_MAX_RANKS];
+  int32_t nranks, rank;
+  int32_t reserved[2];
+} MkEpPeers;
 enum { /* MK_OP_STREAM */ MK_P_ST_W = 0, MK_P_ST_OUT = 1, MK_I_ST_ROWS = 0, MK_I_ST_K = 1 };
 
 typedef struct MkConfig {
@@ -171,6 +196,15 @@ int mk_status(MkHandle* h, MkStatus* out);
 int mk_reset(MkHandle* h);
 /* Trace records of the last launch (trace enabled): copies up to cap records, *n = count. */
 int mk_trace(MkHandle* h, MkTraceRecord* out, int64_t cap, int64_t* n);
+/* Expert parallelism buffers (no counterpart in the reference, which exchanged through NCCL):
+   device memory that peer processes can map (cudaMalloc, zeroed), its 64-byte IPC handle, and a
+   peer's buffer opened in this process (peer access enabled lazily); close and free release them. */
+int mk_ep_alloc(int32_t device, size_t bytes, void** dev_ptr);
+int mk_ep_free(void* dev_ptr);
+int mk_ep_ipc_handle(void* dev_ptr, void* handle64);
+int mk_ep_ipc_open(int32_t device, const void* handle64, void** peer_ptr);
+int mk_ep_ipc_close(void* peer_ptr);
+
 /* Replace the consumer-side dependencies of operator op_index (by default: the previous
    operator) with n (1 or 2) earlier operators of the same iteration; before mk_finalize. Every
    operator must still lead to the last one. Lets independent operators overlap (the MoE's

@@ -1,0 +1,81 @@
+"""Host side of expert parallelism, without a GPU: the per-rank plans (disjoint owned expert
+ranges, the exchange operators in place) and the IPC handle exchange of fleet.ep.EpGroup over a
+two-rank gloo group with the library calls faked."""
+import os
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT / "fleet-amd-task_b200"))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_plans_partition_the_experts(world):
+    from fleet import build_graph as B
+    from fleet import mk
+    from fleet.pack_weights import REAL_DIMS as d
+    owned = []
+    for rank in range(world):
+        plan, ops = B.dry_run(layers=4, ep=(rank, world))
+        assert not plan.chain_violations()
+        labels = [c.label for c in plan.calls]
+        for l in range(1, 4):
+            i13, i2, ic = labels.index(f"L{l}.w13r"), labels.index(f"L{l}.w2_combine"), labels.index(f"L{l}.ep_combine")
+            assert i13 < i2 < ic and labels[ic + 1] == f"L{l + 1}.qkva" if l < 3 else labels[ic + 1] == "head.lm_head"
+            g, w2, ec = ops[i13], ops[i2], ops[ic]
+            assert g["flags"] & mk.F_EP and w2["flags"] & mk.F_EP
+            lo, hi = g["ips"][5], g["ips"][6]
+            assert (w2["ips"][6], w2["ips"][7]) == (lo, hi) and w2["ips"][8] == l - 1 and ec["ips"][2] == l - 1
+            assert ec["type"] == mk.OP_EP_COMBINE and w2["ptrs"][mk.P["w2"]["PEERS"]] == "ep_peers"
+        owned.append((lo, hi))
+    assert sorted(owned) == owned and owned[0][0] == 0 and owned[-1][1] == d.E
+    assert all(a[1] == b[0] for a, b in zip(owned, owned[1:]))
+
+
+def _rank(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from fleet import ep as E
+    from fleet import mk
+    base = 0x100000 * (rank + 1)
+    fake = dict(alloc=iter([base, base + 0x1000]))
+    mk.ep_alloc = lambda dev, n: next(fake["alloc"])
+    mk.ep_free = lambda p: None
+    mk.ep_ipc_handle = lambda p: p.to_bytes(8, "little") * 8
+    mk.ep_ipc_open = lambda dev, h: int.from_bytes(h[:8], "little") + 0x7000000000
+    mk.ep_ipc_close = lambda p: None
+
+    def all_gather(obj):
+        objs = [None] * world
+        dist.all_gather_object(objs, obj)
+        return objs
+
+    g = E.EpGroup(rank, world, 0, 8, 2048, 26, all_gather, table_device="cpu")
+    t = mk.MkEpPeers.from_buffer_copy(bytes(g.table.numpy()))
+    q.put((rank, [t.out8[r] for r in range(world)], [t.counter[r] for r in range(world)], t.nranks, t.rank))
+    g.close()
+    dist.destroy_process_group()
+
+
+def test_ep_group_exchanges_handles_over_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29400 + os.getpid() % 500
+    ps = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, out8, ctr, n, me in res:
+        assert (n, me) == (2, rank)
+        for r in range(2):
+            own = 0x100000 * (r + 1)
+            want_out8 = own if r == rank else own + 0x7000000000
+            assert out8[r] == want_out8 and ctr[r] == want_out8 + 0x1000
