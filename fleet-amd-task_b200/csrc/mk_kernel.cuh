@@ -911,8 +911,8 @@ __device__ void gateup_body(const KernelParams& P, Smem& sm, const OpDev& od, co
 }
 
 // ---- expert down projection per slot, then the weighted combine into x_res ------------------
-// With MK_F_EP the task computes its rank's slots (w2_slots), writes their out8 rows, stores the
-// routed ones into every peer's out8 too and signals the peers' counters; MK_OP_EP_COMBINE adds.
+// With MK_F_EP the task computes its rank's slots (w2_slots), exchanges the routed rows with the
+// same task of every peer rank, and combines all slots of its rows.
 template <int KS>
 __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const TaskDev& t, const Iter& itx,
                         Cons& c) {
@@ -942,7 +942,11 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
   mark_stages(sm, c);
   consumer_sync();
   uint16_t* out8 = P_<uint16_t>(od, MK_P_W2_OUT8);
+  const uint16_t* xin = nullptr;   // EP: the exchange rows (this layer's half)
   if (ep) {
+    // the routed rows this rank computed go to every peer (the same rows of the peer's exchange
+    // buffer), then this task tells the peers' task t and waits until each peer's task t has told
+    // it: the exchange is per task, with no operator boundary
     const MkEpPeers* pe = P_<const MkEpPeers>(od, MK_P_W2_PEERS);
     const int TOPK = (int)I_(od, MK_I_W2_TOPK), nranks = pe->nranks, me = pe->rank;
     // the exchange buffers alternate by layer parity: a peer writes layer l + 2's rows only after
@@ -950,68 +954,48 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
     const size_t half = ((size_t)I_(od, MK_I_W2_LAYER) & 1u) * (size_t)NS * H;
     for (int i = c.tid; i < ws.n * nr_t; i += NUM_CONSUMERS) {
       const int k = i / nr_t, lr = i - k * nr_t, s = ws.slot[k], row = t.a + lr;
+      if (s >= TOPK) continue;
       const uint16_t ob = (uint16_t)f32_to_bf16_bits(row_total<KS>(pbuf, s * nr_t + lr));
-      out8[half + (size_t)s * H + row] = ob;
-      if (s < TOPK)
-        for (int r = 0; r < nranks; ++r)
-          if (r != me) reinterpret_cast<uint16_t*>(pe->out8[r])[half + (size_t)s * H + row] = ob;
+      for (int r = 0; r < nranks; ++r)
+        if (r != me) reinterpret_cast<uint16_t*>(pe->out8[r])[half + (size_t)s * H + row] = ob;
     }
     consumer_sync();
-    if (c.tid == 0) {   // the stores above happen before the peers see the count (system scope)
-      __threadfence_system();
-      const int layer = (int)I_(od, MK_I_W2_LAYER);
-      for (int r = 0; r < nranks; ++r)
-        if (r != me) red_release_sys_add(pe->counter[r] + layer, 1u);
+    if (c.tid == 0) {
+      const size_t ci = (size_t)I_(od, MK_I_W2_LAYER) * MK_EP_MAX_TASKS + (size_t)t.idx;
+      for (int r = 0; r < nranks; ++r)   // release at system scope: the CTA's stores reach the peer first
+        if (r != me) red_release_sys_add(pe->counter[r] + ci, 1u);
+      const uint32_t target = (uint32_t)(nranks - 1) * itx.g;
+      const uint32_t* ctr = pe->counter[me] + ci;
+      const uint64_t t0 = globaltimer();
+      int ok = 1;
+      for (uint32_t n = 0;; ++n) {
+        if ((int32_t)(ld_acquire_sys_u32(ctr) - target) >= 0) break;
+        if ((n & 31u) == 31u && (aborted(P, sm) || (int64_t)(globaltimer() - t0) > P.timeout_ns)) { ok = 0; break; }
+      }
+      if (!ok)
+        report_error(P, sm, *(volatile uint32_t*)&P.status->abort_flag ? MK_DERR_ABORTED : MK_DERR_WAIT_TIMEOUT,
+                     (uint32_t)t.op, (uint32_t)t.idx, 0x20000u | (uint32_t)I_(od, MK_I_W2_LAYER));
+      sm.bcast[2] = ok;
     }
-    return;
+    consumer_sync();
+    if (!sm.bcast[2]) return;
+    xin = reinterpret_cast<const uint16_t*>(pe->out8[me]) + half;
   }
   const float* topk_w = P_<const float>(od, MK_P_W2_TOPKW);
   uint16_t* xres = P_<uint16_t>(od, MK_P_W2_XRES);
+  uint32_t mine = 0;   // slots computed here (the rest come from the exchange rows)
+  for (int k = 0; k < ws.n; ++k) mine |= 1u << ws.slot[k];
   for (int lr = c.tid; lr < nr_t; lr += NUM_CONSUMERS) {
     const int row = t.a + lr;
     float acc = bf16_bits_to_f32(ldcg_u16(xres + row));
     for (int s = 0; s < NS; ++s) {   // numpy_ref.moe_combine's operation order: acc + f32(out * w)
-      const uint32_t ob = f32_to_bf16_bits(row_total<KS>(pbuf, s * nr_t + lr));
+      const uint32_t ob = ((mine >> s) & 1u) ? f32_to_bf16_bits(row_total<KS>(pbuf, s * nr_t + lr))
+                                             : ldcg_u16(xin + (size_t)s * H + row);
       acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(ob), ldcg_f32(topk_w + s)));
       if (out8) out8[(size_t)s * H + row] = (uint16_t)ob;
     }
     xres[row] = (uint16_t)f32_to_bf16_bits(acc);
   }
-}
-
-// ---- expert-parallel combine: wait for the peers' out8 rows, then the slot-order sum ---------
-__device__ void ep_combine_body(const KernelParams& P, Smem& sm, const OpDev& od, const TaskDev& t, const Iter& itx,
-                                Cons& c) {
-  const int H = (int)I_(od, MK_I_EC_H), NS = (int)I_(od, MK_I_EC_SLOTS), layer = (int)I_(od, MK_I_EC_LAYER);
-  const MkEpPeers* pe = P_<const MkEpPeers>(od, MK_P_EC_PEERS);
-  if (c.tid == 0) {
-    // every peer's w2 tasks add 1 per iteration (bounded wait, system scope)
-    const uint32_t target = (uint32_t)(pe->nranks - 1) * (uint32_t)I_(od, MK_I_EC_W2TASKS) * itx.g;
-    const uint32_t* ctr = pe->counter[pe->rank] + layer;
-    const uint64_t t0 = globaltimer();
-    int ok = 1;
-    for (uint32_t n = 0;; ++n) {
-      if ((int32_t)(ld_acquire_sys_u32(ctr) - target) >= 0) break;
-      if ((n & 31u) == 31u && (aborted(P, sm) || (int64_t)(globaltimer() - t0) > P.timeout_ns)) { ok = 0; break; }
-    }
-    if (!ok)
-      report_error(P, sm, *(volatile uint32_t*)&P.status->abort_flag ? MK_DERR_ABORTED : MK_DERR_WAIT_TIMEOUT,
-                   (uint32_t)t.op, (uint32_t)t.idx, 0x20000u | (uint32_t)layer);
-    sm.bcast[2] = ok;
-  }
-  consumer_sync();
-  mark_body(sm, c);
-  if (!sm.bcast[2]) return;
-  const uint16_t* out8 = P_<const uint16_t>(od, MK_P_EC_OUT8) + ((size_t)layer & 1u) * (size_t)NS * H;
-  const float* topk_w = P_<const float>(od, MK_P_EC_TOPKW);
-  uint16_t* xres = P_<uint16_t>(od, MK_P_EC_XRES);
-  for (int row = t.a + c.tid; row < t.b; row += NUM_CONSUMERS) {
-    float acc = bf16_bits_to_f32(ldcg_u16(xres + row));
-    for (int s = 0; s < NS; ++s)   // numpy_ref.moe_combine's operation order: acc + f32(out * w)
-      acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(ldcg_u16(out8 + (size_t)s * H + row)), ldcg_f32(topk_w + s)));
-    xres[row] = (uint16_t)f32_to_bf16_bits(acc);
-  }
-  mark_stages(sm, c);
 }
 
 // ---- stream probe: the ring's bytes, no arithmetic -------------------------------------------
@@ -1079,7 +1063,6 @@ __device__ void run_task(const KernelParams& P, Smem& sm, const OpDev& od, const
       by_parts(I, [&](auto ks) { w2_body<decltype(ks)::value>(P, sm, od, t, itx, c); });
       break;
     }
-    case MK_OP_EP_COMBINE: ep_combine_body(P, sm, od, t, itx, c); break;
     case MK_OP_STREAM: op_stream(P, sm, od, t, itx, c); break;
     default: break;
   }

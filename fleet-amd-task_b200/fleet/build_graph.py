@@ -95,8 +95,9 @@ def gateup_layer(mk, t, input, weight, act, inter, groups, expert, norm, w_norm=
 
 def moe_w2_combine_layer(mk, t, input, weight, mask, topk_w, residual, output, out8=None, ep_range=None, peers=None,
                          topk=None, layer=0):
-    """ep_range (lo, hi): expert parallelism; the task writes its rank's slots' out8 rows (the
-    routed ones into every peer's out8 too, through `peers`) and ep_combine_layer adds them."""
+    """ep_range (lo, hi): expert parallelism; the task computes its rank's slots for its rows,
+    exchanges the routed rows with the same task of every peer (`peers`, fleet/ep.py) and
+    combines all slots (out8 is then not written)."""
     E, H, I = weight.shape
     assert residual.data_ptr() == output.data_ptr(), "the combine adds into x_res in place"
     n_slots = input.shape[0]
@@ -109,14 +110,7 @@ def moe_w2_combine_layer(mk, t, input, weight, mask, topk_w, residual, output, o
                                                 w["XRES"]: output, w["OUT8"]: out8, w["PEERS"]: peers}, ips)
 
 
-def ep_combine_layer(mk, t, out8, topk_w, residual, output, peers, layer, w2_tasks):
-    """Expert parallelism: wait for every peer's out8 rows of `layer`, then x_res += sum w out8 in
-    slot order (numpy_ref.moe_combine)."""
-    assert residual.data_ptr() == output.data_ptr(), "the combine adds into x_res in place"
-    _, n_slots, H = out8.shape
-    c = mk.P["ec"]
-    return mk.make_op(mk.OP_EP_COMBINE, 0, {c["OUT8"]: out8, c["TOPKW"]: topk_w, c["XRES"]: output, c["PEERS"]: peers},
-                      {0: H, 1: n_slots, 2: layer, 3: w2_tasks})
+
 
 
 def stream_layer(mk, t, weight, dummy, dummy_in=None):
@@ -127,7 +121,7 @@ NEW_LAYERS = {
     "embed_layer": embed_layer, "linear_gemv_layer": linear_gemv_layer, "mla_prep_layer": mla_prep_layer,
     "mla_attend_layer": mla_attend_layer, "mla_merge_uv_layer": mla_merge_uv_layer,
     "moe_router_layer": moe_router_layer, "gateup_layer": gateup_layer,
-    "moe_w2_combine_layer": moe_w2_combine_layer, "stream_layer": stream_layer, "ep_combine_layer": ep_combine_layer,
+    "moe_w2_combine_layer": moe_w2_combine_layer, "stream_layer": stream_layer,
 }
 
 
@@ -271,7 +265,6 @@ def build(packed, capture, meta, dims=REAL_DIMS, s_max=1056, layers=27, head=Tru
                             ep=None if ep is None else (ep.rank, ep.world))
     if ep is not None:
         workspaces = dict(workspaces or {})
-        workspaces["ep_out8"] = ep.out8
         workspaces["ep_peers"] = ep.peers
     if stop_after:
         plan.truncate(stop_after)
@@ -282,10 +275,7 @@ def build(packed, capture, meta, dims=REAL_DIMS, s_max=1056, layers=27, head=Tru
     n_cta = num_ctas or torch.cuda.get_device_properties(dev).multi_processor_count
     index = {}
     for i, c in enumerate(plan.calls):
-        kw = call_kwargs(c, host)
-        if c.method == "ep_combine_layer":       # the combine counts the down projection's tasks
-            kw["w2_tasks"] = kernel.tasks(index[kw.pop("w2_label")])
-        op = NEW_LAYERS[c.method](mk, None, **kw)
+        op = NEW_LAYERS[c.method](mk, None, **call_kwargs(c, host))
         if c.beside and op.ntasks == 0:
             # the operators it runs beside keep their CTAs; it takes the rest (tasks are dealt to
             # CTAs in chain order from a rotating start, so the free CTAs are the next ones)
@@ -333,8 +323,7 @@ class FakeTensor:
 
 class FakeMk:
     """Records operators instead of calling the library (the reference's FakeMPK role)."""
-    (OP_EMBED, OP_GEMV, OP_MLA_PREP, OP_MLA_ATTEND, OP_MLA_MERGE_UV, OP_ROUTER, OP_GATEUP, OP_W2_COMBINE, OP_STREAM,
-     OP_EP_COMBINE) = range(1, 11)
+    OP_EMBED, OP_GEMV, OP_MLA_PREP, OP_MLA_ATTEND, OP_MLA_MERGE_UV, OP_ROUTER, OP_GATEUP, OP_W2_COMBINE, OP_STREAM = range(1, 10)
     F_NORM, F_RESIDUAL, F_ARGMAX, F_EXPERT, F_STATIC_IDS, F_EP = 1, 2, 4, 8, 16, 32
 
     def __init__(self):
@@ -365,11 +354,7 @@ def dry_run(dims=REAL_DIMS, s_max=1056, layers=27, head=True, debug=False, stop_
     host = {n: FakeTensor(n, t.shape, t.dtype) for n, t in plan.tensors.items()}
     fmk = FakeMk()
     for c in plan.calls:
-        kw = call_kwargs(c, host)
-        if c.method == "ep_combine_layer":
-            kw.pop("w2_label")
-            kw["w2_tasks"] = 1
-        NEW_LAYERS[c.method](fmk, None, **kw)
+        NEW_LAYERS[c.method](fmk, None, **call_kwargs(c, host))
     set_plan_deps(plan, fmk)
     return plan, fmk.ops
 

@@ -105,7 +105,6 @@ OUTPUT_ARGS = {
     "moe_router_layer": ["h", "topk_w", "routing", "mask", "logits", "route_log"],
     "gateup_layer": ["act", "mid", "h_out"],
     "moe_w2_combine_layer": ["output", "out8"],
-    "ep_combine_layer": ["output"],
     "stream_layer": ["dummy"],
 }
 
@@ -192,7 +191,8 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
     injected FP32 bias [E] to its logits (the skewed/uniform routing of config 3). softmax_scale:
     default q_head_dim^-0.5 times the YaRN mscale^2 of the dims (0.1147213867929261 at REAL_DIMS).
     ep (rank, world): expert parallelism (fleet/ep.py): this rank's routed gate/up and down
-    projection cover its own experts, and an ep_combine waits for the peers' rows."""
+    projection cover its own experts; each down-projection task exchanges its rows with the same
+    task of every peer before it combines."""
     from fleet.capture import softmax_scale as yarn_softmax_scale
     d = dims
     scale = yarn_softmax_scale(d.D_N, d.D_R) if softmax_scale is None else softmax_scale
@@ -226,7 +226,6 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
         p.t("out8", (d.N_SLOTS, d.H))
         p.t("route_log", (route_log_rows, d.L - 1, d.N_SLOTS), "i32")
         if ep is not None:
-            p.t("ep_out8", (2, d.N_SLOTS, d.H))
             p.t("ep_peers", (EP_PEERS_WORDS,), "i32")
     p.op("embed_layer", "prologue.embed", input="tokens", weight="W_embed", output="x_res")
     for l in range(layers):
@@ -287,9 +286,7 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
                      ep_range=rng)
                 p.op("moe_w2_combine_layer", f"L{l}.w2_combine", deps=(f"L{l}.w13r", f"L{l}.w13s"), input="act8",
                      weight=f"W2_{l}", mask="mask", topk_w="topk_w", residual="x_res", output="x_res",
-                     out8="ep_out8", ep_range=rng, peers="ep_peers", topk=d.TOPK, layer=l - 1)
-                p.op("ep_combine_layer", f"L{l}.ep_combine", out8="ep_out8", topk_w="topk_w", residual="x_res",
-                     output="x_res", peers="ep_peers", layer=l - 1, w2_label=f"L{l}.w2_combine")
+                     ep_range=rng, peers="ep_peers", topk=d.TOPK, layer=l - 1)
     if head:
         p.t("w_final_norm", (d.H,), kind="input", source="w_final_norm")
         p.t("W_lm", (d.V, d.H), kind="input", source="W_lm")

@@ -63,10 +63,7 @@ enum MkOpType {
                              layer 0's gang_linear_silu) */
   MK_OP_W2_COMBINE = 8,   /* out8 = W2 act per slot, x += sum w out8     (gang_moe_w2_silu_mi300.cuh
                              + moe_mul_sum_add) */
-  MK_OP_STREAM = 9,       /* read-only bandwidth probe of the weight ring (stream_mi300.cuh:99) */
-  MK_OP_EP_COMBINE = 10   /* expert parallelism: wait until every peer rank has stored its routed
-                             slots' out8 rows here, then x += sum w out8 in slot order (the
-                             exchange + moe_mul_sum_add of the expert-parallel configurations) */
+  MK_OP_STREAM = 9        /* read-only bandwidth probe of the weight ring (stream_mi300.cuh:99) */
 };
 
 /* MkOp.flags */
@@ -77,10 +74,10 @@ enum MkOpType {
 #define MK_F_STATIC_IDS (1 << 4) /* GATEUP: `mask` holds constant expert ids (no wait for a router) */
 #define MK_F_EP (1 << 5)         /* GATEUP / W2_COMBINE: expert parallelism. GATEUP computes only the
                                     routed slots whose expert is in [ep_lo, ep_hi), spread over its
-                                    tasks at run time; W2_COMBINE computes those slots and the shared
-                                    ones, stores the routed slots' out8 rows into every peer's out8
-                                    and signals the peers' counters, and leaves the combine to
-                                    MK_OP_EP_COMBINE */
+                                    tasks at run time. W2_COMBINE task t computes those slots and the
+                                    shared ones for its rows, stores the routed rows into every
+                                    peer's exchange buffer, signals the peers' task-t counters, waits
+                                    for its own (every peer's task t), and combines all slots */
 
 #define MK_MAX_PTRS 16
 #define MK_MAX_IPARAMS 16
@@ -127,13 +124,12 @@ enum { /* MK_OP_W2_COMBINE */ MK_P_W2_ACT = 0, MK_P_W2_W = 1, MK_P_W2_MASK = 2, 
        MK_P_W2_PEERS = 6,   /* MK_F_EP: device MkEpPeers */
        MK_I_W2_H = 0, MK_I_W2_I = 1, MK_I_W2_SLOTS = 2, MK_I_W2_ESTRIDE = 3, MK_I_W2_NEXP = 4,
        MK_I_W2_TOPK = 5, MK_I_W2_EPLO = 6, MK_I_W2_EPHI = 7, MK_I_W2_LAYER = 8 };
-enum { /* MK_OP_EP_COMBINE */ MK_P_EC_OUT8 = 0, MK_P_EC_TOPKW = 1, MK_P_EC_XRES = 2, MK_P_EC_PEERS = 3,
-       MK_I_EC_H = 0, MK_I_EC_SLOTS = 1, MK_I_EC_LAYER = 2, MK_I_EC_W2TASKS = 3 };
-
 /* Expert parallelism: where each rank's exchange buffers are, as this rank maps them (peer
-   pointers opened with mk_ep_ipc_open). out8[r] is rank r's [slots, H] BF16 out8 buffer and
-   counter[r] its array of per-MoE-layer arrival counters (32-bit, monotonic). */
+   pointers opened with mk_ep_ipc_open). out8[r] is rank r's [2][slots][H] BF16 exchange buffer
+   (halves by MoE-layer parity) and counter[r] its [layers][MK_EP_MAX_TASKS] arrival counters
+   (32-bit, monotonic; a peer's down-projection task t adds 1 per iteration). */
 #define MK_EP_MAX_RANKS 8
+#define MK_EP_MAX_TASKS 256
 typedef struct MkEpPeers {
   void* out8[MK_EP_MAX_RANKS];
   uint32_t* counter[MK_EP_MAX_RANKS];

@@ -25,13 +25,13 @@ def test_ep_plans_partition_the_experts(world):
         assert not plan.chain_violations()
         labels = [c.label for c in plan.calls]
         for l in range(1, 4):
-            i13, i2, ic = labels.index(f"L{l}.w13r"), labels.index(f"L{l}.w2_combine"), labels.index(f"L{l}.ep_combine")
-            assert i13 < i2 < ic and labels[ic + 1] == f"L{l + 1}.qkva" if l < 3 else labels[ic + 1] == "head.lm_head"
-            g, w2, ec = ops[i13], ops[i2], ops[ic]
+            i13, i2 = labels.index(f"L{l}.w13r"), labels.index(f"L{l}.w2_combine")
+            assert i13 < i2
+            g, w2 = ops[i13], ops[i2]
             assert g["flags"] & mk.F_EP and w2["flags"] & mk.F_EP
             lo, hi = g["ips"][5], g["ips"][6]
-            assert (w2["ips"][6], w2["ips"][7]) == (lo, hi) and w2["ips"][8] == l - 1 and ec["ips"][2] == l - 1
-            assert ec["type"] == mk.OP_EP_COMBINE and w2["ptrs"][mk.P["w2"]["PEERS"]] == "ep_peers"
+            assert (w2["ips"][6], w2["ips"][7]) == (lo, hi) and w2["ips"][8] == l - 1
+            assert w2["ptrs"][mk.P["w2"]["PEERS"]] == "ep_peers" and mk.P["w2"]["OUT8"] not in w2["ptrs"]
         owned.append((lo, hi))
     assert sorted(owned) == owned and owned[0][0] == 0 and owned[-1][1] == d.E
     assert all(a[1] == b[0] for a, b in zip(owned, owned[1:]))
