@@ -95,7 +95,7 @@ __device__ bool produce_task(const KernelParams& P, Smem& sm, Prod& pr, const Op
       while (gu_next(od, p, gm.b, ch)) {
         int e = 0;
         if (expert) {
-          e = __ldcg(mask + gm.slot[ch.group]);
+          e = __ldcg(mask + gu_slot(gm, ch.group));
           if (e < 0 || e >= nexp) { report_error(P, sm, MK_DERR_BAD_EXPERT, op, task, (uint32_t)e); return false; }
         }
         const uint8_t* src = W + ((size_t)e * (size_t)estride + (size_t)ch.q * 2 * K) * 2;
@@ -112,9 +112,8 @@ __device__ bool produce_task(const KernelParams& P, Smem& sm, Prod& pr, const Op
       const int nexp = (int)I_(od, MK_I_W2_NEXP);
       (void)H;
       (void)NS;
-      const W2Slots ws = w2_slots(od);
-      for (int k = 0; k < ws.n; ++k) {
-        const int e = __ldcg(mask + ws.slot[k]);
+      for (uint32_t sl = w2_slots(od); sl; sl &= sl - 1u) {
+        const int e = __ldcg(mask + (__ffs(sl) - 1));
         if (e < 0 || e >= nexp) { report_error(P, sm, MK_DERR_BAD_EXPERT, op, task, (uint32_t)e); return false; }
         const uint8_t* base = W + (size_t)e * (size_t)estride * 2;
         for (int r = t.a; r < t.b; r += od.rps) {
@@ -581,7 +580,7 @@ __device__ void attend_body(const KernelParams& P, Smem& sm, const OpDev& od, co
   }
   // o: each thread owns pairs of adjacent latent columns and walks the rows in order
   const uint32_t pbaddr = smem_u32(pb);
-  float acc0[2], acc1[2];
+  float acc00 = 0.0f, acc01 = 0.0f, acc10 = 0.0f, acc11 = 0.0f;   // pairs k = 0, 1 (registers, not an array)
   int np = 0;
   for (int i = c.tid, k = 0; i < DC / 2 && k < 2; i += NUM_CONSUMERS, ++k) {
     const uint32_t col = (uint32_t)i * 4u;   // byte offset of the pair in a row
@@ -644,15 +643,15 @@ __device__ void attend_body(const KernelParams& P, Smem& sm, const OpDev& od, co
       s0 = fmaf(lo_f32(v), pp, s0);
       s1 = fmaf(hi_f32(v), pp, s1);
     }
-    acc0[k] = s0;
-    acc1[k] = s1;
+    if (k == 0) { acc00 = s0; acc01 = s1; } else { acc10 = s0; acc11 = s1; }
     np = k + 1;
   }
   consumer_sync();   // l
   const float l = ml[1];
   for (int k = 0; k < np; ++k) {
     const int i = c.tid + k * NUM_CONSUMERS;
-    *reinterpret_cast<float2*>(prow_out + 2 * i) = make_float2(__fdiv_rn(acc0[k], l), __fdiv_rn(acc1[k], l));
+    *reinterpret_cast<float2*>(prow_out + 2 * i) =
+        make_float2(__fdiv_rn(k == 0 ? acc00 : acc10, l), __fdiv_rn(k == 0 ? acc01 : acc11, l));
   }
   if (c.tid == 0) prow_out[DC] = __fadd_rn(ml[0], det_log(l));
   for (int s = 0; s < nst; ++s) release_stage(sm, c);
@@ -901,7 +900,7 @@ __device__ void gateup_body(const KernelParams& P, Smem& sm, const OpDev& od, co
   uint16_t* act = P_<uint16_t>(od, MK_P_GU_ACT);
   uint16_t* mid = P_<uint16_t>(od, MK_P_GU_MID);
   for (int lp = c.tid; lp < gm.b - gm.a; lp += NUM_CONSUMERS) {
-    const int gp = gm.a + lp, g = gm.slot[gp / I], q = gp % I;
+    const int gp = gm.a + lp, g = gu_slot(gm, gp / I), q = gp % I;
     const uint32_t gb = f32_to_bf16_bits(row_total<KS>(pbuf, 2 * lp));
     const uint32_t ub = f32_to_bf16_bits(row_total<KS>(pbuf, 2 * lp + 1));
     const float a = __fmul_rn(det_silu(bf16_bits_to_f32(gb)), bf16_bits_to_f32(ub));
@@ -920,7 +919,8 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
   const uint16_t* act = P_<const uint16_t>(od, MK_P_W2_ACT);
   const int nr_t = t.b - t.a;
   const bool ep = (od.op.flags & MK_F_EP) != 0;
-  const W2Slots ws = w2_slots(od);
+  const uint32_t wsl = w2_slots(od);   // the slots computed here
+  const int wn = __popc(wsl);
   // all slots' activations staged in shared memory with one round of 16-byte loads
   uint16_t* abuf = reinterpret_cast<uint16_t*>(sm.scratch);                         // NS x I
   float* pbuf = reinterpret_cast<float*>(sm.scratch + W2_PBUF_OFF);                  // [NS * rows][KS]
@@ -929,8 +929,8 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
   consumer_sync();
   mark_body(sm, c);
   (void)itx;
-  for (int k = 0; k < ws.n; ++k) {
-    const int s = ws.slot[k];
+  for (uint32_t sl = wsl; sl; sl &= sl - 1u) {
+    const int s = __ffs(sl) - 1;
     const uint4 xv = x_part<KS, true>(abuf + (size_t)s * I, I, c);
     for (int r0 = t.a; r0 < t.b; r0 += od.rps) {
       const int nr = min(od.rps, t.b - r0);
@@ -952,8 +952,8 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
     // the exchange buffers alternate by layer parity: a peer writes layer l + 2's rows only after
     // this rank's layer l + 1 rows reached it, which follows this rank's layer l combine
     const size_t half = ((size_t)I_(od, MK_I_W2_LAYER) & 1u) * (size_t)NS * H;
-    for (int i = c.tid; i < ws.n * nr_t; i += NUM_CONSUMERS) {
-      const int k = i / nr_t, lr = i - k * nr_t, s = ws.slot[k], row = t.a + lr;
+    for (int i = c.tid; i < wn * nr_t; i += NUM_CONSUMERS) {
+      const int k = i / nr_t, lr = i - k * nr_t, s = (int)__fns(wsl, 0u, k + 1), row = t.a + lr;
       if (s >= TOPK) continue;
       const uint16_t ob = (uint16_t)f32_to_bf16_bits(row_total<KS>(pbuf, s * nr_t + lr));
       for (int r = 0; r < nranks; ++r)
@@ -983,8 +983,7 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
   }
   const float* topk_w = P_<const float>(od, MK_P_W2_TOPKW);
   uint16_t* xres = P_<uint16_t>(od, MK_P_W2_XRES);
-  uint32_t mine = 0;   // slots computed here (the rest come from the exchange rows)
-  for (int k = 0; k < ws.n; ++k) mine |= 1u << ws.slot[k];
+  const uint32_t mine = wsl;   // slots computed here (the rest come from the exchange rows)
   for (int lr = c.tid; lr < nr_t; lr += NUM_CONSUMERS) {
     const int row = t.a + lr;
     float acc = bf16_bits_to_f32(ldcg_u16(xres + row));
