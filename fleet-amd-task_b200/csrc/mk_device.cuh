@@ -21,6 +21,9 @@ constexpr int PBUF_OFF = XBUF_BYTES;                       // scratch [8 KB, 32 
 constexpr int W2_PBUF_OFF = 24576;                         // the expert down projection stages all slots'
                                                            // activations in [0, 24 KB), partials after
 constexpr int MAX_ROUTED = 16;                           // N_SLOTS bound (8 at DeepSeek-V2-Lite)
+// the down projection's slot weights and slot outputs follow its activations (16-byte aligned)
+__host__ __device__ constexpr int w2_aux_off(int ns, int inter) { return (ns * inter * 2 + 15) / 16 * 16; }
+__host__ __device__ constexpr int w2_aux_bytes(int ns, int rows) { return (MAX_ROUTED + ns * rows) * 4; }
 
 // ---- tables uploaded by the host ----------------------------------------------------------
 

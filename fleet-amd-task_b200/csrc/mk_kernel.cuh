@@ -312,15 +312,16 @@ __device__ void gemv_body(const KernelParams& P, Smem& sm, const OpDev& od, cons
       if (sm.wbest_v[k] > v || (sm.wbest_v[k] == v && sm.wbest_i[k] < i)) { v = sm.wbest_v[k]; i = sm.wbest_i[k]; }
     P.amax_val[t.idx] = v;
     P.amax_idx[t.idx] = i;
-    __threadfence();
+    // acq_rel: releases the partials above (and, through the barrier, the CTA's rows), acquires
+    // every earlier task's
     const uint32_t old = atom_add_acqrel(&P.arrive[t.op], 1u);
     sm.bcast[1] = (old + 1u == (uint32_t)od.ntasks * itx.g) ? 1 : 0;
   }
   consumer_sync();
   if (!sm.bcast[1] || c.warp != 0) return;
   // the last task to arrive: warp 0 reduces all tasks' bests (lanes load in parallel; the
-  // maximum with ties to the lower index does not depend on the order)
-  __threadfence();
+  // maximum with ties to the lower index does not depend on the order). Thread 0's acquire and
+  // the barrier order the loads after every task's release.
   float v = -__int_as_float(0x7F800000);
   int i = 0x7FFFFFFF;
   for (int k = c.lane; k < od.ntasks; k += 32) {
@@ -784,16 +785,14 @@ __device__ void router_body(const KernelParams& P, Smem& sm, const OpDev& od, co
     logits[t.a + lr] = l;
   }
   consumer_sync();
-  if (c.tid == 0) {
-    __threadfence();
+  if (c.tid == 0) {   // acq_rel: releases the CTA's logits (through the barrier), acquires the others'
     const uint32_t old = atom_add_acqrel(&P.arrive[t.op], 1u);
     sm.bcast[1] = (old + 1u == (uint32_t)od.ntasks * itx.g) ? 1 : 0;
   }
   consumer_sync();
   mark_stages(sm, c);
   if (!sm.bcast[1] || c.warp != 0) return;
-  // the last task to arrive routes (one warp; E <= 32 * 8)
-  __threadfence();
+  // the last task to arrive routes (one warp; E <= 32 * 8), after thread 0's acquire and the barrier
   constexpr int EK = 8;
   float lv[EK], pv[EK];
   float mx = -__int_as_float(0x7F800000);
@@ -921,11 +920,19 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
   const bool ep = (od.op.flags & MK_F_EP) != 0;
   const uint32_t wsl = w2_slots(od);   // the slots computed here
   const int wn = __popc(wsl);
-  // all slots' activations staged in shared memory with one round of 16-byte loads
+  // shared scratch: all slots' activations, the slot weights, the slots' BF16 outputs, partials
   uint16_t* abuf = reinterpret_cast<uint16_t*>(sm.scratch);                         // NS x I
+  float* wk = reinterpret_cast<float*>(sm.scratch + w2_aux_off(NS, I));              // NS slot weights
+  float* obs = wk + MAX_ROUTED;                                                      // [NS][rows]
   float* pbuf = reinterpret_cast<float*>(sm.scratch + W2_PBUF_OFF);                  // [NS * rows][KS]
+  // one round of loads before the stages: the activations (16-byte pieces), the slot weights and
+  // each row's residual, so the epilogue waits for no global load
+  const float* topk_w = P_<const float>(od, MK_P_W2_TOPKW);
+  uint16_t* xres = P_<uint16_t>(od, MK_P_W2_XRES);
   for (int i = c.tid; i < NS * I / 8; i += NUM_CONSUMERS)
     reinterpret_cast<uint4*>(abuf)[i] = ldcg16(act + (size_t)i * 8);
+  if (c.tid < NS) wk[c.tid] = ldcg_f32(topk_w + c.tid);
+  const float res = c.tid < nr_t ? bf16_bits_to_f32(ldcg_u16(xres + t.a + c.tid)) : 0.0f;
   consumer_sync();
   mark_body(sm, c);
   (void)itx;
@@ -941,7 +948,15 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
   }
   mark_stages(sm, c);
   consumer_sync();
+  // the slots computed here: BF16 outputs, one (slot, row) per thread
   uint16_t* out8 = P_<uint16_t>(od, MK_P_W2_OUT8);
+  for (int i = c.tid; i < wn * nr_t; i += NUM_CONSUMERS) {
+    const int k = i / nr_t, lr = i - k * nr_t, s = (int)__fns(wsl, 0u, k + 1);
+    const uint32_t ob = f32_to_bf16_bits(row_total<KS>(pbuf, s * nr_t + lr));
+    obs[s * nr_t + lr] = bf16_bits_to_f32(ob);
+    if (out8) out8[(size_t)s * H + t.a + lr] = (uint16_t)ob;
+  }
+  consumer_sync();
   const uint16_t* xin = nullptr;   // EP: the exchange rows (this layer's half)
   if (ep) {
     // the routed rows this rank computed go to every peer (the same rows of the peer's exchange
@@ -953,11 +968,11 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
     // this rank's layer l + 1 rows reached it, which follows this rank's layer l combine
     const size_t half = ((size_t)I_(od, MK_I_W2_LAYER) & 1u) * (size_t)NS * H;
     for (int i = c.tid; i < wn * nr_t; i += NUM_CONSUMERS) {
-      const int k = i / nr_t, lr = i - k * nr_t, s = (int)__fns(wsl, 0u, k + 1), row = t.a + lr;
+      const int k = i / nr_t, lr = i - k * nr_t, s = (int)__fns(wsl, 0u, k + 1);
       if (s >= TOPK) continue;
-      const uint16_t ob = (uint16_t)f32_to_bf16_bits(row_total<KS>(pbuf, s * nr_t + lr));
+      const uint16_t ob = (uint16_t)f32_to_bf16_bits(obs[s * nr_t + lr]);
       for (int r = 0; r < nranks; ++r)
-        if (r != me) reinterpret_cast<uint16_t*>(pe->out8[r])[half + (size_t)s * H + row] = ob;
+        if (r != me) reinterpret_cast<uint16_t*>(pe->out8[r])[half + (size_t)s * H + t.a + lr] = ob;
     }
     consumer_sync();
     if (c.tid == 0) {
@@ -981,17 +996,12 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
     if (!sm.bcast[2]) return;
     xin = reinterpret_cast<const uint16_t*>(pe->out8[me]) + half;
   }
-  const float* topk_w = P_<const float>(od, MK_P_W2_TOPKW);
-  uint16_t* xres = P_<uint16_t>(od, MK_P_W2_XRES);
-  const uint32_t mine = wsl;   // slots computed here (the rest come from the exchange rows)
   for (int lr = c.tid; lr < nr_t; lr += NUM_CONSUMERS) {
     const int row = t.a + lr;
-    float acc = bf16_bits_to_f32(ldcg_u16(xres + row));
+    float acc = lr == c.tid ? res : bf16_bits_to_f32(ldcg_u16(xres + row));
     for (int s = 0; s < NS; ++s) {   // numpy_ref.moe_combine's operation order: acc + f32(out * w)
-      const uint32_t ob = ((mine >> s) & 1u) ? f32_to_bf16_bits(row_total<KS>(pbuf, s * nr_t + lr))
-                                             : ldcg_u16(xin + (size_t)s * H + row);
-      acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(ob), ldcg_f32(topk_w + s)));
-      if (out8) out8[(size_t)s * H + row] = (uint16_t)ob;
+      const float ob = ((wsl >> s) & 1u) ? obs[s * nr_t + lr] : bf16_bits_to_f32(ldcg_u16(xin + (size_t)s * H + row));
+      acc = __fadd_rn(acc, __fmul_rn(ob, wk[s]));
     }
     xres[row] = (uint16_t)f32_to_bf16_bits(acc);
   }
