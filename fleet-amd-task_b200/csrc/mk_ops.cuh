@@ -141,10 +141,13 @@ __device__ __forceinline__ float row_dot(const uint4 (&xr)[MAXV], const uint8_t*
   return warp_butterfly(__fadd_rn(a0, a1));
 }
 
+// Warp maximum of finite or infinite FP32 values as one integer reduction: the key flips the
+// magnitude bits of negative values, so signed keys order like the values (a -0 / +0 tie may
+// come back as either zero, which no caller distinguishes: they subtract the maximum).
 __device__ __forceinline__ float warp_max_f32(float a) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-  return a;
+  const int b = __float_as_int(a);
+  const int m = __reduce_max_sync(0xffffffffu, b >= 0 ? b : b ^ 0x7FFFFFFF);
+  return __int_as_float(m >= 0 ? m : m ^ 0x7FFFFFFF);
 }
 
 // ---- RMSNorm of a BF16 row into shared memory (all 256 consumer threads) ----------------------
