@@ -612,6 +612,7 @@ __device__ void attend_body(const KernelParams& P, Smem& sm, const OpDev& od, co
         for (; slot < n; ++slot, ++r) fma_pv1(s0, s1, lds32(base + (uint32_t)slot * 1024u), lds16(pbhaddr + (uint32_t)r * 2u));
       }
     }
+    if constexpr (!FAST) {
     for (; r + 4 <= nstr; r += 4) {          // four rows' loads in flight, then in order
       uint32_t v[4];
 #pragma unroll
@@ -634,6 +635,7 @@ __device__ void attend_body(const KernelParams& P, Smem& sm, const OpDev& od, co
       s0 = fmaf(lo_f32(v), pp, s0);
       s1 = fmaf(hi_f32(v), pp, s1);
     }
+    }   // FAST: the stage loop above covered every streamed row
     if (a.has_pos) {
       const uint32_t v = lds32(xaddr + col);
       const float pp = ldsf(pbaddr + (uint32_t)nstr * 4u);
