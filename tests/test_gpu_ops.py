@@ -183,6 +183,36 @@ def test_mla_prep_attend_merge(mk, B, pos):
     assert_bits_equal(attn, R.mla_merge_uv(want, np32(W_uv), pos, split=split), "attn")
 
 
+# Config C2, the MLA decode-attention sweep: contexts 1K..32K with N(0,1) BF16 q and latent KV
+# (seed 3). At 1K the split factors 8 / 16 / 32 are splits of 128 / 64 / 32 rows; longer contexts
+# keep 128-row splits (a split's rows must fit the weight ring), 32 to 256 of them per head, which
+# the merge adds in order.
+@pytest.mark.parametrize("ctx,split", [(1024, 128), (1024, 64), (1024, 32), (4096, 128), (16384, 128), (32768, 128)])
+def test_mla_attend_merge_long_context(mk, B, ctx, split):
+    nh, d_r, d_c, d_v, hg = 16, 64, 512, 128, 1
+    s_max = ctx
+    n_splits = -(-s_max // split)
+    pos = ctx - 1
+    g = gen(3)
+    ql = rnd_bf16(g, nh, d_c)
+    qp = rnd_bf16(g, nh, d_r)
+    c_kv = rnd_bf16(g, s_max, d_c)
+    k_pe = rnd_bf16(g, s_max, d_r)
+    W_uv = rnd_bf16(g, nh, d_v, d_c, std=0.05)
+    from fleet.capture import softmax_scale
+    from fleet.graph_plan import partials_row
+    partials = torch.zeros((n_splits, nh, partials_row(d_c)), dtype=torch.float32, device=DEV)
+    attn = torch.zeros(nh * d_v, dtype=torch.bfloat16, device=DEV)
+    scale = softmax_scale(128, d_r)
+    ops = [B.mla_attend_layer(mk, None, ql, qp, c_kv, k_pe, partials, scale, split, n_splits, hg),
+           B.mla_merge_uv_layer(mk, None, partials, W_uv, attn, split, n_splits)]
+    run_ops(mk, ops, step=pos - 1)
+    want = R.mla_attend(np32(ql), np32(qp), np32(c_kv), np32(k_pe), pos, scale, split=split, n_splits=n_splits)
+    got = partials.cpu().numpy()
+    assert np.array_equal(got[:, :, :d_c + 1].view(np.uint32), want.view(np.uint32)), "partials differ"
+    assert_bits_equal(attn, R.mla_merge_uv(want, np32(W_uv), pos, split=split), "attn")
+
+
 def _router_inputs(g, E=64, H=2048):
     x = rnd_bf16(g, H)
     w_norm = (1.0 + 0.5 * torch.randn(H, generator=g, device=DEV)).to(torch.bfloat16)
