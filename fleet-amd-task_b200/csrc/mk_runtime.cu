@@ -275,8 +275,9 @@ static int add_op_impl(MkHandle* h, const MkOp& in, int32_t* op_index) {
       if (in.flags & MK_F_EP) {
         // the ranges are computed at run time over the owned slots; the host's are placeholders
         if (int e = req((in.flags & MK_F_EXPERT) && !(in.flags & MK_F_STATIC_IDS) && G <= MAX_ROUTED &&
-                            in.ip[MK_I_GU_EPLO] >= 0 && in.ip[MK_I_GU_EPHI] > in.ip[MK_I_GU_EPLO],
-                        "gateup EP: routed experts, slots <= 16, an owned expert range"))
+                            in.ip[MK_I_GU_EPWORLD] >= 1 && in.ip[MK_I_GU_EPWORLD] <= MK_EP_MAX_RANKS &&
+                            in.ip[MK_I_GU_EPRANK] >= 0 && in.ip[MK_I_GU_EPRANK] < in.ip[MK_I_GU_EPWORLD],
+                        "gateup EP: routed experts, slots <= 16, a rank of at most 8"))
           return e;
       }
       if ((in.flags & MK_F_EXPERT) && !(in.flags & MK_F_STATIC_IDS))
@@ -295,9 +296,11 @@ static int add_op_impl(MkHandle* h, const MkOp& in, int32_t* op_index) {
       split_even(ranges, (int)H, t);
       if (in.flags & MK_F_EP) {
         if (int e = req(in.ptr[MK_P_W2_PEERS] && !in.ptr[MK_P_W2_OUT8] && in.ip[MK_I_W2_TOPK] >= 1 &&
-                            in.ip[MK_I_W2_TOPK] <= NS && in.ip[MK_I_W2_EPHI] > in.ip[MK_I_W2_EPLO] &&
+                            in.ip[MK_I_W2_TOPK] <= NS && in.ip[MK_I_W2_EPWORLD] >= 1 &&
+                            in.ip[MK_I_W2_EPWORLD] <= MK_EP_MAX_RANKS && in.ip[MK_I_W2_EPRANK] >= 0 &&
+                            in.ip[MK_I_W2_EPRANK] < in.ip[MK_I_W2_EPWORLD] &&
                             in.ip[MK_I_W2_LAYER] >= 0 && t <= MK_EP_MAX_TASKS,
-                        "w2 EP: peers (no out8), topk, an owned expert range, at most 256 tasks"))
+                        "w2 EP: peers (no out8), topk, a rank of at most 8, at most 256 tasks"))
           return e;
       }
       if (int e = req(w2_aux_off((int)NS, (int)I) + w2_aux_bytes((int)NS, (int)max_range(ranges)) <= W2_PBUF_OFF &&

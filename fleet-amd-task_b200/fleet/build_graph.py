@@ -76,36 +76,36 @@ def moe_router_layer(mk, t, input, w_norm, w_gate, h, topk_w, routing, mask, log
 
 
 def gateup_layer(mk, t, input, weight, act, inter, groups, expert, norm, w_norm=None, mask=None, mid=None, h_out=None,
-                 eps=G.RMS_EPS, static_ids=False, ep_range=None):
+                 eps=G.RMS_EPS, static_ids=False, ep=None):
     """static_ids: the mask holds constant expert ids (the shared experts), so the weights stream
-    without waiting for a router. ep_range (lo, hi): expert parallelism, only the slots whose
-    expert is in [lo, hi), spread over the tasks at run time."""
+    without waiting for a router. ep (rank, world): expert parallelism by slot, only the routed
+    slots s with s mod world = rank, spread over the tasks."""
     K = weight.shape[-1]
     estride = weight.shape[-2] * K if weight.dim() == 3 else 0
     nexp = weight.shape[0] if weight.dim() == 3 else 1
     flags = (mk.F_EXPERT if expert else 0) | (mk.F_NORM if norm else 0) | (mk.F_STATIC_IDS if static_ids else 0)
     ips = {0: K, 1: inter, 2: groups, 3: estride, 4: nexp}
-    if ep_range is not None:
+    if ep is not None:
         flags |= mk.F_EP
-        ips.update({5: ep_range[0], 6: ep_range[1]})
+        ips.update({5: ep[0], 6: ep[1]})
     u = mk.P["gu"]
     return mk.make_op(mk.OP_GATEUP, flags, {u["X"]: input, u["WNORM"]: w_norm, u["W"]: weight, u["MASK"]: mask,
                                             u["MID"]: mid, u["ACT"]: act, u["HOUT"]: h_out}, ips, {0: eps})
 
 
-def moe_w2_combine_layer(mk, t, input, weight, mask, topk_w, residual, output, out8=None, ep_range=None, peers=None,
+def moe_w2_combine_layer(mk, t, input, weight, mask, topk_w, residual, output, out8=None, ep=None, peers=None,
                          topk=None, layer=0):
-    """ep_range (lo, hi): expert parallelism; the task computes its rank's slots for its rows,
-    exchanges the routed rows with the same task of every peer (`peers`, fleet/ep.py) and
-    combines all slots (out8 is then not written)."""
+    """ep (rank, world): expert parallelism by slot; the task computes its rank's routed slots and
+    the shared ones for its rows, exchanges the routed rows with the same task of every peer
+    (`peers`, fleet/ep.py) and combines all slots (out8 is then not written)."""
     E, H, I = weight.shape
     assert residual.data_ptr() == output.data_ptr(), "the combine adds into x_res in place"
     n_slots = input.shape[0]
     w = mk.P["w2"]
     flags, ips = 0, {0: H, 1: I, 2: n_slots, 3: H * I, 4: E}
-    if ep_range is not None:
+    if ep is not None:
         flags = mk.F_EP
-        ips.update({5: topk, 6: ep_range[0], 7: ep_range[1], 8: layer})
+        ips.update({5: topk, 6: ep[0], 7: ep[1], 8: layer})
     return mk.make_op(mk.OP_W2_COMBINE, flags, {w["ACT"]: input, w["W"]: weight, w["MASK"]: mask, w["TOPKW"]: topk_w,
                                                 w["XRES"]: output, w["OUT8"]: out8, w["PEERS"]: peers}, ips)
 

@@ -1,19 +1,22 @@
-"""Expert parallelism over the ranks of one node (one process per GPU).
+"""Expert parallelism over the ranks of one node (one process per GPU), by slot.
 
-Every rank runs the whole decode graph: attention, the dense layer 0, the embedding, the head, the
-router and the shared experts are replicated (the router is deterministic, so all ranks route
-alike). Rank r owns the routed experts [r E / N, (r + 1) E / N): its gate/up computes only the
-routed slots whose expert it owns. Each down-projection task stores its rows of those slots into
-the same rows of every peer's exchange buffer, adds one to the peer's counter for (layer, task),
-waits until every peer's same task has done the same, and adds the eight slots in slot order, so
-the result is the one-GPU result bit for bit.
+Every rank runs the whole decode graph: attention, the dense layer 0, the embedding, the head,
+the router and the shared experts are replicated (the router is deterministic, so all ranks route
+alike). Every rank holds every expert's weights (31 GB in all, far below one GPU's 180 GB), so the
+six routed slots of a token are dealt round-robin: rank r of N computes the routed slots s with
+s mod N = r, whatever experts the router picked, and the ranks stay balanced at batch 1 (sharding
+by expert id leaves a rank idle whenever the top-6 experts cluster on another). Each
+down-projection task stores its rows of its rank's routed slots into the same rows of every
+peer's exchange buffer, adds one to the peer's counter for (layer, task), waits until every
+peer's same task has done the same, and adds the eight slots in slot order, so the result is the
+one-GPU result bit for bit.
 
 The exchange buffers are plain device memory from the library (cudaMalloc), mapped into the peers
 with CUDA IPC; no multicast object is involved. Handles travel over the process group."""
 import ctypes
 
 from fleet import mk
-from fleet.graph_plan import EP_PEERS_WORDS, ep_expert_range as expert_range  # noqa: F401
+from fleet.graph_plan import EP_PEERS_WORDS, ep_slots  # noqa: F401
 
 
 class DeviceBuffer:
@@ -73,8 +76,9 @@ class EpGroup:
         assert ctypes.sizeof(table) == 4 * EP_PEERS_WORDS
         self.peers = DeviceBuffer(self.table.data_ptr(), (EP_PEERS_WORDS,), 4, "ep_peers")
 
-    def experts(self, n_experts):
-        return expert_range(self.rank, self.world, n_experts)
+    def slots(self, topk):
+        """The routed slots this rank computes."""
+        return ep_slots(self.rank, self.world, topk)
 
     def close(self):
         """Release the mappings and the buffers; call after a barrier of all ranks (a peer may

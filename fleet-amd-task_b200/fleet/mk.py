@@ -31,9 +31,9 @@ P = dict(
     rt=dict(X=0, WNORM=1, WGATE=2, HOUT=3, LOGITS=4, TOPKW=5, ROUTING=6, MASK=7, ROUTELOG=8, BIAS=9),
     rt_i=dict(H=0, E=1, TOPK=2, NFORCED=3, LAYER=4, LOGSTRIDE=5, LOGROWS=6),
     gu=dict(X=0, WNORM=1, W=2, MASK=3, MID=4, ACT=5, HOUT=6),
-    gu_i=dict(K=0, I=1, GROUPS=2, ESTRIDE=3, NEXP=4, EPLO=5, EPHI=6),
+    gu_i=dict(K=0, I=1, GROUPS=2, ESTRIDE=3, NEXP=4, EPRANK=5, EPWORLD=6),
     w2=dict(ACT=0, W=1, MASK=2, TOPKW=3, XRES=4, OUT8=5, PEERS=6),
-    w2_i=dict(H=0, I=1, SLOTS=2, ESTRIDE=3, NEXP=4, TOPK=5, EPLO=6, EPHI=7, LAYER=8),
+    w2_i=dict(H=0, I=1, SLOTS=2, ESTRIDE=3, NEXP=4, TOPK=5, EPRANK=6, EPWORLD=7, LAYER=8),
     st=dict(W=0, OUT=1), st_i=dict(ROWS=0, K=1),
 )
 

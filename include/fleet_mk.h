@@ -72,12 +72,14 @@ enum MkOpType {
 #define MK_F_ARGMAX (1 << 2)     /* GEMV: greedy argmax of the output into tokens[pos + 1] */
 #define MK_F_EXPERT (1 << 3)     /* GATEUP: groups are the routed slots of `mask` */
 #define MK_F_STATIC_IDS (1 << 4) /* GATEUP: `mask` holds constant expert ids (no wait for a router) */
-#define MK_F_EP (1 << 5)         /* GATEUP / W2_COMBINE: expert parallelism. GATEUP computes only the
-                                    routed slots whose expert is in [ep_lo, ep_hi), spread over its
-                                    tasks at run time. W2_COMBINE task t computes those slots and the
-                                    shared ones for its rows, stores the routed rows into every
-                                    peer's exchange buffer, signals the peers' task-t counters, waits
-                                    for its own (every peer's task t), and combines all slots */
+#define MK_F_EP (1 << 5)         /* GATEUP / W2_COMBINE: expert parallelism by slot over N ranks, each
+                                    holding every expert's weights: rank r computes the routed slots
+                                    s with s mod N = r (GATEUP spreads their pairs over its tasks;
+                                    the shared slots stay on every rank). W2_COMBINE task t computes
+                                    those slots and the shared ones for its rows, stores the routed
+                                    rows into every peer's exchange buffer, signals the peers'
+                                    task-t counters, waits for its own (every peer's task t), and
+                                    combines all slots */
 
 #define MK_MAX_PTRS 16
 #define MK_MAX_IPARAMS 16
@@ -118,12 +120,12 @@ enum { /* MK_OP_ROUTER */ MK_P_RT_X = 0, MK_P_RT_WNORM = 1, MK_P_RT_WGATE = 2, M
 enum { /* MK_OP_GATEUP */ MK_P_GU_X = 0, MK_P_GU_WNORM = 1, MK_P_GU_W = 2, MK_P_GU_MASK = 3,
        MK_P_GU_MID = 4, MK_P_GU_ACT = 5, MK_P_GU_HOUT = 6,
        MK_I_GU_K = 0, MK_I_GU_I = 1, MK_I_GU_GROUPS = 2, MK_I_GU_ESTRIDE = 3, MK_I_GU_NEXP = 4,
-       MK_I_GU_EPLO = 5, MK_I_GU_EPHI = 6 };
+       MK_I_GU_EPRANK = 5, MK_I_GU_EPWORLD = 6 };
 enum { /* MK_OP_W2_COMBINE */ MK_P_W2_ACT = 0, MK_P_W2_W = 1, MK_P_W2_MASK = 2, MK_P_W2_TOPKW = 3,
        MK_P_W2_XRES = 4, MK_P_W2_OUT8 = 5,
        MK_P_W2_PEERS = 6,   /* MK_F_EP: device MkEpPeers */
        MK_I_W2_H = 0, MK_I_W2_I = 1, MK_I_W2_SLOTS = 2, MK_I_W2_ESTRIDE = 3, MK_I_W2_NEXP = 4,
-       MK_I_W2_TOPK = 5, MK_I_W2_EPLO = 6, MK_I_W2_EPHI = 7, MK_I_W2_LAYER = 8 };
+       MK_I_W2_TOPK = 5, MK_I_W2_EPRANK = 6, MK_I_W2_EPWORLD = 7, MK_I_W2_LAYER = 8 };
 /* Expert parallelism: where each rank's exchange buffers are, as this rank maps them (peer
    pointers opened with mk_ep_ipc_open). out8[r] is rank r's [2][slots][H] BF16 exchange buffer
    (halves by MoE-layer parity) and counter[r] its [layers][MK_EP_MAX_TASKS] arrival counters

@@ -1,5 +1,5 @@
-"""Host side of expert parallelism, without a GPU: the per-rank plans (disjoint owned expert
-ranges, the exchange operators in place) and the IPC handle exchange of fleet.ep.EpGroup over a
+"""Host side of expert parallelism, without a GPU: the per-rank plans (the routed slots dealt
+round-robin over the ranks, the exchange operators in place) and the IPC handle exchange of fleet.ep.EpGroup over a
 two-rank gloo group with the library calls faked."""
 import os
 import sys
@@ -15,11 +15,12 @@ sys.path.insert(0, str(ROOT / "fleet-amd-task_b200"))
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_ep_plans_partition_the_experts(world):
+def test_ep_plans_deal_the_slots(world):
     from fleet import build_graph as B
     from fleet import mk
+    from fleet.graph_plan import ep_slots
     from fleet.pack_weights import REAL_DIMS as d
-    owned = []
+    dealt = []
     for rank in range(world):
         plan, ops = B.dry_run(layers=4, ep=(rank, world))
         assert not plan.chain_violations()
@@ -29,12 +30,15 @@ def test_ep_plans_partition_the_experts(world):
             assert i13 < i2
             g, w2 = ops[i13], ops[i2]
             assert g["flags"] & mk.F_EP and w2["flags"] & mk.F_EP
-            lo, hi = g["ips"][5], g["ips"][6]
-            assert (w2["ips"][6], w2["ips"][7]) == (lo, hi) and w2["ips"][8] == l - 1
+            assert (g["ips"][5], g["ips"][6]) == (rank, world)
+            assert (w2["ips"][6], w2["ips"][7]) == (rank, world) and w2["ips"][8] == l - 1
+            assert w2["ips"][5] == d.TOPK
             assert w2["ptrs"][mk.P["w2"]["PEERS"]] == "ep_peers" and mk.P["w2"]["OUT8"] not in w2["ptrs"]
-        owned.append((lo, hi))
-    assert sorted(owned) == owned and owned[0][0] == 0 and owned[-1][1] == d.E
-    assert all(a[1] == b[0] for a, b in zip(owned, owned[1:]))
+        dealt += ep_slots(rank, world, d.TOPK)
+    # every routed slot on exactly one rank, and no rank more than one slot above another
+    assert sorted(dealt) == list(range(d.TOPK))
+    counts = [len(ep_slots(r, world, d.TOPK)) for r in range(world)]
+    assert max(counts) - min(counts) <= 1
 
 
 def _rank(rank, world, port, q):
