@@ -309,11 +309,13 @@ def cpu_baseline(packed, capture, meta, d, plan, budget_s):
 
 def roofline(d, ms_per_token, ctx, bw_peak, peak_kind, world=1):
     """Algorithmic HBM bytes of one GPU's launch per token over its time: with expert parallelism
-    a rank reads the replicated weights and 1/world of the routed experts' (on average)."""
+    rank 0 (the busiest) reads the replicated weights and ceil(TOPK / world) of the TOPK routed
+    slots' expert weights."""
     from fleet.pack_weights import active_bytes_per_token, routed_bytes_per_token
     algo = active_bytes_per_token(d, ctx=ctx)
     if world > 1:
-        algo -= routed_bytes_per_token(d) * (world - 1) // world
+        mine = -(-d.TOPK // world)
+        algo -= routed_bytes_per_token(d) * (d.TOPK - mine) // d.TOPK
     achieved = algo / (ms_per_token * 1e-3) / 1e9
     traffic = None
     f = ROOT / "profiles" / "decode_traffic.txt"
@@ -347,7 +349,8 @@ def run_ours(args):
             dist.all_gather_object(objs, obj)
             return objs
 
-        # expert parallelism: rank r owns routed experts [r E/N, (r+1) E/N); the rest is replicated
+        # expert parallelism by slot: rank r computes the routed slots s with s mod N = r; every
+        # rank holds every expert's weights and runs the rest of the graph
         ep = EpGroup(rank, ws, local, D.N_SLOTS, D.H, args.layers - 1, all_gather)
     d, packed, capture, meta, mpk, host, plan, t_setup = build_model(args, device, args.layers, ep)
     stream = torch.cuda.Stream(device=device)
@@ -397,8 +400,8 @@ def run_ours(args):
         "data": "synthetic: seeded BF16 weights N(0, 0.02), norms 1.0; seeded N(0,1) latent cache of 1,023 rows",
         "config": {"workload": "C1: 27-layer DeepSeek-V2-Lite-shaped greedy decode, batch 1, 1 launch/token",
                    "layers": args.layers, "ctx": [ctx0, ctx0 + args.steps - 1], "parallelism":
-                   f"expert parallel x{ws}: routed experts {64 // ws} per GPU, the rest replicated; "
-                   "per-token latency is the max over ranks" if ws > 1 else "1 GPU",
+                   f"expert parallel x{ws}: the 6 routed slots dealt round-robin over the GPUs, the rest "
+                   "replicated; per-token latency is the max over ranks" if ws > 1 else "1 GPU",
                    "l2": "no flush: 4.9 GB read per step >> 126 MB L2",
                    "tokens_per_s": round(1e3 / ms, 2)},
         "tokens_per_s": round(1e3 / ms, 2),
