@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=27)
+    ap.add_argument("--ctx", type=int, default=N_PROMPT,
+                    help="prompt length (latent-cache rows + 1); 8192 is config 4's context (cache seed 5)")
     ap.add_argument("--cpu-sample-s", type=float, default=20.0, help="bound of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--trace", action="store_true", help="record per-task stamps (not timed)")
@@ -182,12 +184,14 @@ def build_model(args, device, layers, ep=None):
     from fleet.pack_weights import REAL_DIMS, synthetic_packed
 
     d = REAL_DIMS
-    s_max = N_PROMPT + args.warmup + args.steps + E2E_STEPS + 2
+    n_prompt = args.ctx
+    s_max = n_prompt + args.warmup + args.steps + E2E_STEPS + 2
     t0 = time.time()
     packed = synthetic_packed(d, layers=layers, head=True, seed=0, device=device)
-    capture = make_capture(d, layers, s_max, N_PROMPT - 1, seed=1, device=device)
-    prompt = torch.randint(0, d.V, (N_PROMPT,), generator=torch.Generator().manual_seed(2)).tolist()
-    meta = B.make_meta(torch, s_max, prompt, N_PROMPT, device=device)
+    # config 1 (1K context): cache seed 1; config 4 (8K context): cache seed 5
+    capture = make_capture(d, layers, s_max, n_prompt - 1, seed=1 if n_prompt == N_PROMPT else 5, device=device)
+    prompt = torch.randint(0, d.V, (n_prompt,), generator=torch.Generator().manual_seed(2)).tolist()
+    meta = B.make_meta(torch, s_max, prompt, n_prompt, device=device)
     mpk, host, plan = B.build(packed, capture, meta, dims=d, s_max=s_max, layers=layers, head=True,
                               trace=args.trace, ep=ep)
     mpk.compile()
@@ -236,7 +240,7 @@ def time_e2e(mpk, meta, steps, torch, stream):
     return e0.elapsed_time(e1) / steps, wall
 
 
-def cpu_baseline(packed, capture, meta, d, plan, budget_s):
+def cpu_baseline(packed, capture, meta, d, plan, budget_s, n_prompt=N_PROMPT):
     """The oracle (the reference's NumPy path, restated) on this host's cores for a bounded
     sample of one decode token: embedding, layer 0 (dense), MoE layers 1..m and the head, timed
     per part and extrapolated to the 26 MoE layers of a token."""
@@ -264,7 +268,7 @@ def cpu_baseline(packed, capture, meta, d, plan, budget_s):
     m_layers = 3
     m = OracleModel(d, get, get_expert, softmax_scale=softmax_scale(d.D_N, d.D_R), split=plan.split,
                     layers=m_layers)
-    pos = N_PROMPT - 1
+    pos = n_prompt - 1
     for l in range(m_layers):
         cache[f"c_kv_{l}"] = np32(capture[f"c_kv_{l}"])
         cache[f"k_pe_{l}"] = np32(capture[f"k_pe_{l}"])
@@ -354,7 +358,7 @@ def run_ours(args):
         ep = EpGroup(rank, ws, local, D.N_SLOTS, D.H, args.layers - 1, all_gather)
     d, packed, capture, meta, mpk, host, plan, t_setup = build_model(args, device, args.layers, ep)
     stream = torch.cuda.Stream(device=device)
-    mpk.step = N_PROMPT - 2
+    mpk.step = args.ctx - 2
     for _ in range(args.warmup):
         mpk.launch(1, stream)
     torch.cuda.synchronize()
@@ -382,7 +386,7 @@ def run_ours(args):
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_baseline(packed, capture, meta, d, plan, args.cpu_sample_s)
+            cpu = cpu_baseline(packed, capture, meta, d, plan, args.cpu_sample_s, args.ctx)
         except MemoryError as e:            # the host could not hold the sample's weights
             cpu = {"value": None, "unit": "ms/token", "error": f"MemoryError: {e}"}
     if dist:
@@ -397,8 +401,11 @@ def run_ours(args):
         "metric": METRIC, "value": round(ms, 4), "unit": "ms/token", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: seeded BF16 weights N(0, 0.02), norms 1.0; seeded N(0,1) latent cache of 1,023 rows",
-        "config": {"workload": "C1: 27-layer DeepSeek-V2-Lite-shaped greedy decode, batch 1, 1 launch/token",
+        "data": f"synthetic: seeded BF16 weights N(0, 0.02), norms 1.0; seeded N(0,1) latent cache of "
+                f"{args.ctx - 1:,} rows",
+        "config": {"workload": ("C1: 27-layer DeepSeek-V2-Lite-shaped greedy decode, batch 1, 1 launch/token"
+                                if args.ctx == N_PROMPT else
+                                f"C4-shaped: the C1 model at {args.ctx}-token context, batch 1, 1 launch/token"),
                    "layers": args.layers, "ctx": [ctx0, ctx0 + args.steps - 1], "parallelism":
                    f"expert parallel x{ws}: the 6 routed slots dealt round-robin over the GPUs, the rest "
                    "replicated; per-token latency is the max over ranks" if ws > 1 else "1 GPU",

@@ -91,3 +91,27 @@ def test_decode_launch_per_token_equals_one_launch():
     want_ids, _, rec, _ = oracle_run(d, packed, capture, meta, cache0, plan, layers, n_run, pos0)
     assert ids == want_ids
     assert_bits_equal(host["logits"][0], rec["head.logits"], "logits")
+
+
+def test_decode_8k_context_matches_oracle():
+    """Config 4's context on one GPU: 8,191 cached rows (seed 5), so every layer's attention runs
+    65 splits of 128 rows per head and the merge combines all of them; a dense layer and a MoE
+    layer, two greedy iterations in one launch, bit for bit against the oracle."""
+    layers, iters = 2, 2
+    d, packed, capture, meta, cache0, mpk, host, plan, pos0 = build_model(layers, iters, n_past=8191, seed=4)
+    assert plan.n_splits >= 65
+    mpk.compile()
+    meta["step"].fill_(pos0 - 1)
+    mpk()
+    st = mpk.status()
+    assert st["error"] == 0, st
+    ids = meta["tokens"][0, pos0 + 1: pos0 + 1 + iters].tolist()
+    want_ids, routes, rec, cache = oracle_run(d, packed, capture, meta, cache0, plan, layers, iters, pos0)
+    assert ids == want_ids
+    rl = host["route_log"].cpu().numpy()
+    for i in range(iters):
+        assert rl[i, 0, :d.TOPK].tolist() == routes[i][0], i
+    for l in range(layers):
+        got = host[f"c_kv_{l}"][pos0:pos0 + iters].float().cpu().numpy()
+        assert np.array_equal(got, cache[f"c_kv_{l}"][pos0:pos0 + iters]), l
+    assert_bits_equal(host["logits"][0], rec["head.logits"], "logits")
