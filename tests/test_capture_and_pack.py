@@ -74,3 +74,15 @@ def test_synthetic_deterministic():
     assert float(a["W_qkva_1"].float().std()) < 0.03
     assert torch.all(a["w_norm1_0"] == 1.0)
     assert sum(v.numel() * v.element_size() for v in a.values()) == P.packed_bytes(d)
+
+
+def test_auto_head_group():
+    """One attention task per head at 1K context; at long context heads share a task (and its
+    streamed cache rows) as long as every CTA still gets a task."""
+    from fleet.graph_plan import auto_head_group, build_plan
+    assert auto_head_group(16, 9) == 1          # 1K context: 144 tasks
+    assert auto_head_group(16, 33) == 2         # 4K: 264 tasks
+    assert auto_head_group(16, 65) == 4         # 8K: 260 tasks
+    assert auto_head_group(16, 257) == 16       # 32K: 257 tasks
+    assert build_plan(s_max=8200, layers=2).head_group == 4
+    assert build_plan(s_max=1056, layers=2).head_group == 1

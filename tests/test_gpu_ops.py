@@ -186,10 +186,13 @@ def test_mla_prep_attend_merge(mk, B, pos):
 # Config C2, the MLA decode-attention sweep: contexts 1K..32K with N(0,1) BF16 q and latent KV
 # (seed 3). At 1K the split factors 8 / 16 / 32 are splits of 128 / 64 / 32 rows; longer contexts
 # keep 128-row splits (a split's rows must fit the weight ring), 32 to 256 of them per head, which
-# the merge adds in order.
-@pytest.mark.parametrize("ctx,split", [(1024, 128), (1024, 64), (1024, 32), (4096, 128), (16384, 128), (32768, 128)])
-def test_mla_attend_merge_long_context(mk, B, ctx, split):
-    nh, d_r, d_c, d_v, hg = 16, 64, 512, 128, 1
+# the merge adds in order. A head group > 1 (the plan's choice at long context) runs several heads
+# of one split in one task over the same ring stages: the same partials, bit for bit.
+@pytest.mark.parametrize("ctx,split,hg", [(1024, 128, 1), (1024, 64, 1), (1024, 32, 1), (4096, 128, 1),
+                                          (4096, 128, 2), (8192, 128, 4), (16384, 128, 1), (16384, 128, 8),
+                                          (32768, 128, 1)])
+def test_mla_attend_merge_long_context(mk, B, ctx, split, hg):
+    nh, d_r, d_c, d_v = 16, 64, 512, 128
     s_max = ctx
     n_splits = -(-s_max // split)
     pos = ctx - 1
