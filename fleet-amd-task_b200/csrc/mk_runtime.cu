@@ -204,7 +204,8 @@ static int add_op_impl(MkHandle* h, const MkOp& in, int32_t* op_index) {
       if (int e = req(NS * S >= in.ip[MK_I_ATT_SMAX], "attend: n_splits * split < s_max")) return e;
       const int rps = (int)(STAGE_BYTES / ((DC + DR) * 2));
       if (int e = req(div_up(S, rps) <= NSTAGES, "attend: a split must fit the ring")) return e;
-      if (int e = req(S % 4 == 0 && 4096 + (3 * S + 4) * 4 + S * 2 <= SCRATCH_BYTES && (DC + DR) * 2 <= 4096,
+      if (int e = req(S % 4 == 0 && 4096 + 2 * (((3 * S + 4) * 4 + S * 2 + 15) / 16 * 16) <= SCRATCH_BYTES &&
+                          (DC + DR) * 2 <= 4096,
                       "attend: scores exceed scratch")) return e;
       if (int e = req(in.ip[MK_I_ATT_PROW] >= DC + 1 && in.ip[MK_I_ATT_PROW] % 4 == 0 &&
                           ((uintptr_t)in.ptr[MK_P_ATT_PARTIALS] & 15) == 0,
