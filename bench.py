@@ -50,7 +50,9 @@ def parse():
                     help="prompt length (latent-cache rows + 1); 8192 is config 4's context (cache seed 5)")
     ap.add_argument("--cpu-sample-s", type=float, default=20.0, help="bound of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--trace", action="store_true", help="record per-task stamps (not timed)")
+    ap.add_argument("--trace", action="store_true",
+                    help="record per-task %%globaltimer stamps and print a per-operator breakdown of the last "
+                         "token to stderr (the timed numbers then include the stamping)")
     return ap.parse_args()
 
 
@@ -210,6 +212,56 @@ def time_steps(mpk, meta, steps, torch, stream):
     torch.cuda.synchronize()
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     return per
+
+
+def trace_summary(mpk, plan, out=sys.stderr):
+    """Per-operator breakdown of the last launch's trace (one token): for each operator of a middle
+    layer its task count, the most tasks one CTA ran, and the median task's prologue (activations
+    loaded), stages (weights consumed) and epilogue (outputs, release); then, per operator kind,
+    the median over the middle layers of how much it extends the token's critical path (its last
+    task's end minus the latest end of every operator before it)."""
+    import statistics as st
+    recs = mpk.kernel.trace()
+    labels = [c.label for c in plan.calls]
+    by = {}
+    for (op, task, cta, it, t_ready, t_end, t_body, t_stages, wait) in recs:
+        by.setdefault(op, []).append((t_ready, t_end, t_body, t_stages, cta))
+    if not by:
+        return
+    ends = {op: max(r[1] for r in v) for op, v in by.items()}
+    layers = sorted({int(lb[1:].split(".")[0]) for lb in labels if lb.startswith("L")})
+    mid = layers[len(layers) // 2] if layers else None
+    print(f"trace of one token: operators of layer {mid} (us; medians over tasks)", file=out)
+    print("%-18s %6s %7s %8s %8s %8s" % ("operator", "tasks", "max/cta", "prologue", "stages", "epilogue"), file=out)
+    for op in sorted(by):
+        if not labels[op].startswith(f"L{mid}."):
+            continue
+        v = by[op]
+        per_cta = {}
+        for r in v:
+            per_cta[r[4]] = per_cta.get(r[4], 0) + 1
+        pro = st.median([(r[2] - r[0]) / 1e3 for r in v if r[2]]) if any(r[2] for r in v) else 0.0
+        stg = st.median([(r[3] - r[2]) / 1e3 for r in v if r[3] and r[2]]) if any(r[3] for r in v) else 0.0
+        epi = st.median([(r[1] - (r[3] or r[2] or r[0])) / 1e3 for r in v])
+        print("%-18s %6d %7d %8.2f %8.2f %8.2f" % (labels[op], len(v), max(per_cta.values()), pro, stg, epi), file=out)
+    order = sorted(by)
+    kinds = {}
+    for i in range(1, len(order)):
+        lab = labels[order[i]]
+        if not lab.startswith("L"):
+            continue
+        l = int(lab[1:].split(".")[0])
+        if l < 2 or l > layers[-1] - 1:
+            continue
+        prev = max(ends[o] for o in order[:i])
+        kinds.setdefault(lab.split(".", 1)[1], []).append(max(0.0, (ends[order[i]] - prev) / 1e3))
+    print("critical-path share per operator kind (us, median over the middle layers):", file=out)
+    total = 0.0
+    for k, v in kinds.items():
+        total += st.median(v)
+        print("  %-14s %7.2f" % (k, st.median(v)), file=out)
+    t0 = min(r[0] for v in by.values() for r in v)
+    print("  per layer      %7.2f; whole token %.1f" % (total, (max(ends.values()) - t0) / 1e3), file=out)
 
 
 def time_e2e(mpk, meta, steps, torch, stream):
@@ -375,6 +427,8 @@ def run_ours(args):
     st = mpk.status()
     ms = sum(per) / len(per)
     e2e_ms, e2e_wall = time_e2e(mpk, meta, E2E_STEPS, torch, stream)
+    if args.trace and rank == 0:
+        trace_summary(mpk, plan)
     st = mpk.status()
     if dist:
         t = torch.tensor([ms, e2e_ms], device=device)
