@@ -86,3 +86,28 @@ def test_auto_head_group():
     assert auto_head_group(16, 257) == 16       # 32K: 257 tasks
     assert build_plan(s_max=8200, layers=2).head_group == 4
     assert build_plan(s_max=1056, layers=2).head_group == 1
+
+
+def test_checkpoint_loader_matches_state_dict(golden, tmp_path):
+    """The real-checkpoint loader (pack_all over a sharded safetensors directory, the reference's
+    fleet/pack_weights.py:275-339 role) gives the same packed tensors as packing the state dict:
+    the tiny reference model's weights written as a two-shard HF checkpoint."""
+    from safetensors.torch import save_file
+    fx = golden("hf_tiny.npz")
+    cfg = json.loads(str(fx["config"]))
+    d = P.Dims.from_config(cfg)
+    sd = {k[2:]: torch.from_numpy(fx[k].astype(np.int16)).view(torch.bfloat16) for k in fx.files if k.startswith("w:")}
+    names = sorted(sd)
+    shards = {"model-00001-of-00002.safetensors": names[: len(names) // 2],
+              "model-00002-of-00002.safetensors": names[len(names) // 2:]}
+    weight_map = {}
+    for fname, keys in shards.items():
+        save_file({k: sd[k].contiguous() for k in keys}, str(tmp_path / fname))
+        weight_map.update({k: fname for k in keys})
+    (tmp_path / "model.safetensors.index.json").write_text(json.dumps({"weight_map": weight_map}))
+    (tmp_path / "config.json").write_text(json.dumps(cfg))
+    got = P.pack_all(tmp_path)
+    want = P.pack_state_dict(d, sd)
+    assert got.keys() == want.keys()
+    for k in want:
+        assert got[k].dtype == torch.bfloat16 and torch.equal(got[k], want[k]), k
