@@ -506,7 +506,7 @@ def run_reference(args):
     v = sum(vals) / len(vals)
     out = {"metric": METRIC, "value": round(v, 2), "unit": "ms/token", "n_gpus": ws, "steps": len(vals),
            "warmup": 0, "ms_per_step": round(v, 2), "higher_is_better": False, "impl": "reference",
-           "vs_baseline": None, "dtype": "f64-accumulated bf16 (oracle port)", "data": "synthetic",
+           "vs_baseline": None, "dtype": "bf16 weights, FP32 sums in the specified orders (oracle port)", "data": "synthetic",
            "config": {"workload": "C1: 27-layer DeepSeek-V2-Lite-shaped greedy decode, batch 1 (CPU oracle port)"},
            "cpu_baseline": {"value": round(v, 2), "unit": "ms/token", "cores": cpu["cores"], "kind": "port",
                             "sample": cpu["sample"]},
