@@ -50,6 +50,8 @@ def parse():
                     help="prompt length (latent-cache rows + 1); 8192 is config 4's context (cache seed 5)")
     ap.add_argument("--cpu-sample-s", type=float, default=20.0, help="bound of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--routing", default="natural", choices=["natural", "uniform", "zipf"],
+                    help="config 3's injected router logits (seed 4): uniform, or Zipf s=1.2 over the experts")
     ap.add_argument("--trace", action="store_true",
                     help="record per-task %%globaltimer stamps and print a per-operator breakdown of the last "
                          "token to stderr (the timed numbers then include the stamping)")
@@ -194,8 +196,12 @@ def build_model(args, device, layers, ep=None):
     capture = make_capture(d, layers, s_max, n_prompt - 1, seed=1 if n_prompt == N_PROMPT else 5, device=device)
     prompt = torch.randint(0, d.V, (n_prompt,), generator=torch.Generator().manual_seed(2)).tolist()
     meta = B.make_meta(torch, s_max, prompt, n_prompt, device=device)
+    routing = getattr(args, "routing", "natural")
+    if routing != "natural":
+        from fleet.capture import router_biases
+        capture.update(router_biases(d, layers, routing, seed=4, device=device))
     mpk, host, plan = B.build(packed, capture, meta, dims=d, s_max=s_max, layers=layers, head=True,
-                              trace=args.trace, ep=ep)
+                              trace=args.trace, ep=ep, logit_bias=routing != "natural")
     mpk.compile()
     torch.cuda.synchronize()
     return d, packed, capture, meta, mpk, host, plan, time.time() - t0
@@ -463,7 +469,7 @@ def run_ours(args):
                    "layers": args.layers, "ctx": [ctx0, ctx0 + args.steps - 1], "parallelism":
                    f"expert parallel x{ws}: the 6 routed slots dealt round-robin over the GPUs, the rest "
                    "replicated; per-token latency is the max over ranks" if ws > 1 else "1 GPU",
-                   "l2": "no flush: 4.9 GB read per step >> 126 MB L2",
+                   "l2": "no flush: 4.9 GB read per step >> 126 MB L2", "routing": args.routing,
                    "tokens_per_s": round(1e3 / ms, 2)},
         "tokens_per_s": round(1e3 / ms, 2),
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms/token", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,

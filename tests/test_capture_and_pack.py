@@ -111,3 +111,17 @@ def test_checkpoint_loader_matches_state_dict(golden, tmp_path):
     assert got.keys() == want.keys()
     for k in want:
         assert got[k].dtype == torch.bfloat16 and torch.equal(got[k], want[k]), k
+
+
+def test_router_biases_zipf_and_uniform():
+    """Config 3's injected routing: seeded, one bias per MoE layer, Zipf-shaped or zero."""
+    d = P.Dims(H=64, NH=2, D_N=16, D_R=8, D_V=16, D_C=32, V=256, L=4, I_DENSE=96, I_MOE=32, E=64, TOPK=6, N_SHARED=2)
+    z = C.router_biases(d, 4, "zipf", device="cpu")
+    assert sorted(z) == ["router_bias_1", "router_bias_2", "router_bias_3"]
+    b = z["router_bias_1"].numpy()
+    assert b.dtype == np.float32 and b.shape == (64,)
+    assert np.isclose(b.max(), 3.0) and np.allclose(np.sort(b)[::-1], 3.0 / np.arange(1, 65) ** 1.2, rtol=1e-6)
+    assert np.array_equal(C.router_biases(d, 4, "zipf", device="cpu")["router_bias_2"].numpy(),
+                          z["router_bias_2"].numpy())
+    assert not np.array_equal(z["router_bias_1"].numpy(), z["router_bias_2"].numpy())
+    assert all(float(t.abs().sum()) == 0.0 for t in C.router_biases(d, 4, "uniform", device="cpu").values())
