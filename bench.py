@@ -184,18 +184,14 @@ class ClockSampler:
 def build_model(args, device, layers, ep=None):
     import torch
     from fleet import build_graph as B
-    from fleet.capture import make_capture
-    from fleet.pack_weights import REAL_DIMS, synthetic_packed
+    from fleet.workload import greedy_decode
 
-    d = REAL_DIMS
-    n_prompt = args.ctx
-    s_max = n_prompt + args.warmup + args.steps + E2E_STEPS + 2
     t0 = time.time()
-    packed = synthetic_packed(d, layers=layers, head=True, seed=0, device=device)
     # config 1 (1K context): cache seed 1; config 4 (8K context): cache seed 5
-    capture = make_capture(d, layers, s_max, n_prompt - 1, seed=1 if n_prompt == N_PROMPT else 5, device=device)
-    prompt = torch.randint(0, d.V, (n_prompt,), generator=torch.Generator().manual_seed(2)).tolist()
-    meta = B.make_meta(torch, s_max, prompt, n_prompt, device=device)
+    w = greedy_decode(device, n_prompt=args.ctx, new_tokens=args.warmup + args.steps + E2E_STEPS, layers=layers,
+                      extra_rows=2)
+    d, packed, capture, s_max, n_prompt = w.dims, w.packed, w.capture, w.s_max, w.n_prompt
+    meta = B.make_meta(torch, s_max, w.prompt, n_prompt, device=device)
     routing = getattr(args, "routing", "natural")
     if routing != "natural":
         from fleet.capture import router_biases
@@ -205,6 +201,18 @@ def build_model(args, device, layers, ep=None):
     mpk.compile()
     torch.cuda.synchronize()
     return d, packed, capture, meta, mpk, host, plan, time.time() - t0
+
+
+def ids_check(meta, args):
+    """The decoded tokens against the CPU oracle's 32 greedy ids of config 1
+    (tests/golden/c1_greedy_ids.json): None when the workload is not config 1's."""
+    f = ROOT / "tests" / "golden" / "c1_greedy_ids.json"
+    if not f.exists() or args.ctx != N_PROMPT or args.layers != 27 or args.routing != "natural":
+        return None
+    want = json.loads(f.read_text())["ids"]
+    got = meta["tokens"][0, N_PROMPT:N_PROMPT + len(want)].tolist()
+    n = min(len(want), args.warmup + args.steps + E2E_STEPS)
+    return {"ids_match": got[:n] == want[:n], "compared": n}
 
 
 def time_steps(mpk, meta, steps, torch, stream):
@@ -436,6 +444,7 @@ def run_ours(args):
     if args.trace and rank == 0:
         trace_summary(mpk, plan)
     st = mpk.status()
+    ids = ids_check(meta, args)
     if dist:
         t = torch.tensor([ms, e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -479,6 +488,7 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
         "device_status": st["error_name"],
+        "ids": ids,
         "setup_s": round(t_setup, 1),
         "ms_per_step_minmax": [round(min(per), 4), round(max(per), 4)],
     }

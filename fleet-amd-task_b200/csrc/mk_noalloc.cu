@@ -124,8 +124,10 @@ __global__ void __launch_bounds__(NA_THREADS) na_attend_kernel(NaArgs a) {
 }
 
 // one block per head: merge the live splits into o (BF16), then attn[h, v] = W_uv[h, v] . o as
-// the persistent kernel's row dot (lane l takes 8-value vectors l + 32 j, even values into a0,
-// odd into a1, then a0 + a1 and the butterfly)
+// the persistent kernel's row dot: the row is KS equal parts of at most 256 values (KS 1 for
+// d_c <= 256, else 2); in each part lane l takes the part's 8-value vector l, adds the even
+// products into a0 and the odd ones into a1, then a0 + a1 and the butterfly gives the part's sum;
+// the part sums are added in part order
 __global__ void __launch_bounds__(NA_THREADS) na_merge_kernel(NaArgs a) {
   __shared__ __align__(16) uint16_t ob[NA_MAX_DC];
   const int h = blockIdx.x;
@@ -143,21 +145,24 @@ __global__ void __launch_bounds__(NA_THREADS) na_merge_kernel(NaArgs a) {
     ob[c] = (uint16_t)f32_to_bf16_bits(__fdiv_rn(num, den));
   }
   __syncthreads();
+  const int ks = a.d_c <= 256 ? 1 : 2, lp = a.d_c / ks;
   for (int v = warp; v < a.d_v; v += NA_THREADS / 32) {
     const uint16_t* wrow = a.w_uv + ((size_t)h * a.d_v + v) * a.d_c;
-    float a0 = 0.0f, a1 = 0.0f;
-    for (int jj = 0; jj < NA_MAX_DC / 256; ++jj) {
-      const int vec = lane + 32 * jj;
-      if (vec * 8 < a.d_c) {
+    float d = 0.0f;
+    for (int p = 0; p < ks; ++p) {
+      float a0 = 0.0f, a1 = 0.0f;
+      if (lane * 8 < lp) {
+        const int base = p * lp + lane * 8;
         for (int t = 0; t < 8; ++t) {
-          const float prod_w = bf16_bits_to_f32(wrow[vec * 8 + t]);
-          const float prod_x = bf16_bits_to_f32((uint32_t)ob[vec * 8 + t]);
-          if (t % 2 == 0) a0 = fmaf(prod_w, prod_x, a0);
-          else a1 = fmaf(prod_w, prod_x, a1);
+          const float w = bf16_bits_to_f32(wrow[base + t]);
+          const float x = bf16_bits_to_f32((uint32_t)ob[base + t]);
+          if (t % 2 == 0) a0 = fmaf(w, x, a0);
+          else a1 = fmaf(w, x, a1);
         }
       }
+      const float part = warp_butterfly(__fadd_rn(a0, a1));
+      d = p == 0 ? part : __fadd_rn(d, part);
     }
-    const float d = warp_butterfly(__fadd_rn(a0, a1));
     if (lane == 0) a.attn[(size_t)h * a.d_v + v] = (uint16_t)f32_to_bf16_bits(d);
   }
 }

@@ -27,7 +27,10 @@ Methods (published, restated here from the mathematics):
   2t (1 + t^2/3 + t^4/5 + t^6/7 + t^8/9) (Abramowitz & Stegun 4.1.27; |t| <= 0.1716 so the
   remainder is < 3e-9 relative), plus e ln2 with the same split of ln2.
 """
+import ctypes
 import math
+import os
+from pathlib import Path
 
 import numpy as np
 
@@ -141,11 +144,38 @@ def butterfly(a):
     return a[..., 0]
 
 
+def vals(a):
+    """BF16 data as float32 values: uint16 arrays are BF16 bit patterns (as device tensors copied
+    with a 16-bit view), anything else is converted to float32."""
+    a = np.asarray(a)
+    return from_bf16_bits(a) if a.dtype == np.uint16 else np.asarray(a, F32)
+
+
 def dot_rows(W, x):
     """FP32 dot products of the rows of W [..., N, K] with x [K] in the kernels' order.
-    W and x hold BF16 values (so each product is exact). Returns float32 [..., N]."""
-    W = np.asarray(W, F32)
-    x = np.asarray(x, F32)
+    W holds BF16 values (float32, or uint16 bit patterns) and x BF16 values (so each product is
+    exact). Returns float32 [..., N]. Uses the C restatement (detdot.c) when it is built; it
+    computes the same bits as dot_rows_np."""
+    L = _od()
+    W = np.asarray(W)
+    if L is not None and W.dtype in (np.uint16, np.float32) and W.ndim >= 1:
+        K = W.shape[-1]
+        gemv_parts(K)
+        Wc = np.ascontiguousarray(W)
+        xc = np.ascontiguousarray(vals(x))
+        assert xc.shape == (K,), (xc.shape, K)
+        lead = Wc.shape[:-1]
+        out = np.empty(int(np.prod(lead, dtype=np.int64)), F32)
+        fn = L.od_dot_rows_bf16 if Wc.dtype == np.uint16 else L.od_dot_rows_f32
+        fn(Wc.ctypes.data, out.size, K, xc.ctypes.data, out.ctypes.data)
+        return out.reshape(lead)
+    return dot_rows_np(W, x)
+
+
+def dot_rows_np(W, x):
+    """dot_rows in numpy: the specification the C restatement follows."""
+    W = vals(W)
+    x = vals(x)
     K = W.shape[-1]
     ks, kp, maxv = gemv_parts(K)
     lead = W.shape[:-1]
@@ -277,6 +307,34 @@ def det_log(x):
     y = np.where(x == np.inf, F32(np.inf), y)
     y = np.where((x < 0) | np.isnan(x), F32(np.nan), y)
     return y.astype(F32)
+
+
+# ---------------------------------------------------------------------------------------------
+# the C restatement of the hot loops (oracle/detdot.c, built by oracle/Makefile)
+
+_OD_LIB = None
+
+
+def _od():
+    """The loaded detdot library, or None (not built, or ORACLE_NUMPY=1): numpy is used then."""
+    global _OD_LIB
+    if _OD_LIB is None:
+        path = Path(__file__).resolve().with_name("libdetdot.so")
+        if os.environ.get("ORACLE_NUMPY") == "1" or not path.exists():
+            _OD_LIB = False
+        else:
+            L = ctypes.CDLL(str(path))
+            vp, i64, i32, f = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+            L.od_set_consts.argtypes = [vp]
+            L.od_dot_rows_bf16.argtypes = [vp, i64, i64, vp, vp]
+            L.od_dot_rows_f32.argtypes = [vp, i64, i64, vp, vp]
+            L.od_det_exp.argtypes, L.od_det_exp.restype = [f], f
+            L.od_det_log.argtypes, L.od_det_log.restype = [f], f
+            L.od_mla_attend.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, f, i32, i32, vp]
+            consts = np.array([LOG2E, LN2_HI, LN2_LO, SQRT2, EXP_LO, EXP_HI] + EXP_C + LOG_C, F32)
+            L.od_set_consts(consts.ctypes.data)
+            _OD_LIB = L
+    return _OD_LIB or None
 
 
 def silu(x):

@@ -12,12 +12,14 @@ explains: every FP32 sum runs in the kernels' specified order, and exp/log are d
 routines. So the CUDA kernels must agree bit for bit, and the reference's own functions agree
 within their own tolerances (tests/test_oracle_pins.py checks both).
 
-Array conventions: BF16 tensors are float32 arrays holding BF16 values (as numpy_ref does).
+Array conventions: BF16 tensors are float32 arrays holding BF16 values (as numpy_ref does); weights
+may also be uint16 arrays of BF16 bit patterns (device tensors copied as 16-bit words), which the
+row dots read directly.
 """
 import numpy as np
 
-from oracle.detmath import (F32, F64, bf16, block_sum, butterfly, det_exp, det_log, dot_rows, lane_sum,
-                            seq_sum, silu)
+from oracle.detmath import (F32, F64, _od, bf16, block_sum, butterfly, det_exp, det_log, dot_rows, lane_sum,
+                            seq_sum, silu, vals)
 
 __all__ = ["bf16", "rmsnorm", "rope", "mla_prep", "mla_attend", "merge_partials", "mla_merge_uv",
            "moe_router", "moe_router_norm", "moe_w13", "moe_w2", "silu", "linear", "linear_norm",
@@ -39,12 +41,12 @@ def rmsnorm(x, w, eps=1e-6):
     """DeepseekV2RMSNorm on BF16 inputs (numpy_ref.py:54-60; modeling_deepseek.py:94-108).
     FP32 sum of squares in the 256-thread block order (detmath.block_sum), divided by n; then
     FP32 1/sqrt(var + eps), the normalised value rounded to BF16, times the BF16 weight, rounded."""
-    x = np.asarray(x, F32)
+    x = vals(x)
     n = x.shape[-1]
     var = (block_sum((x * x).astype(F32)) / F32(n)).astype(F32)[..., None]
     r = (F32(1.0) / np.sqrt((var + F32(eps)).astype(F32))).astype(F32)
     xn = bf16((x * r).astype(F32))
-    return bf16((np.asarray(w, F32) * xn).astype(F32))
+    return bf16((vals(w) * xn).astype(F32))
 
 
 def rope(x, cos_row, sin_row):
@@ -56,8 +58,8 @@ def rope(x, cos_row, sin_row):
     x = x.reshape(*x.shape[:-1], d // 2, 2).swapaxes(-1, -2).reshape(*x.shape[:-1], d)
     h = d // 2
     rot = np.concatenate([-x[..., h:], x[..., :h]], axis=-1)
-    return bf16(bf16((x * np.asarray(cos_row, F32)).astype(F32))
-                + bf16((rot * np.asarray(sin_row, F32)).astype(F32)))
+    return bf16(bf16((x * vals(cos_row)).astype(F32))
+                + bf16((rot * vals(sin_row)).astype(F32)))
 
 
 # ---------------------------------------------------------------------------------------------
@@ -98,7 +100,7 @@ def mla_prep(qkva, w_kv_norm, W_uk, cos_row, sin_row, *, nh=16, d_n=128, d_r=64,
     k_pe_row = rope(k_pe_raw, cos_row, sin_row)
     q_nope, q_pe = q[:, :d_n], q[:, d_n:]
     q_pe = rope(q_pe, cos_row, sin_row)
-    W_uk = np.asarray(W_uk, F32)
+    W_uk = np.asarray(W_uk)
     ql = np.stack([dot_rows(W_uk[h].T, q_nope[h]) for h in range(nh)])
     return c_row, k_pe_row, bf16(ql), q_pe
 
@@ -139,14 +141,20 @@ def mla_attend(ql_nope, q_pe, c_kv, k_pe, step, softmax_scale, *, split=32, n_sp
       o = (FP32 sum over rows, in row order, of bf16(p) c_kv) / l;  lse = m + det_log(l)
     An empty split stores o = 0 and lse = -inf. Returns partials [n_splits, nh, d_c + 1] FP32
     (and the scaled scores [nh, step + 1] with debug_scores)."""
-    ql_nope = np.asarray(ql_nope, F32)
-    q_pe = np.asarray(q_pe, F32)
-    c_kv = np.asarray(c_kv, F32)
-    k_pe = np.asarray(k_pe, F32)
+    ql_nope = np.ascontiguousarray(vals(ql_nope))
+    q_pe = np.ascontiguousarray(vals(q_pe))
+    c_kv = np.ascontiguousarray(vals(c_kv))
+    k_pe = np.ascontiguousarray(vals(k_pe))
     nh, d_c = ql_nope.shape
     s_max = c_kv.shape[0]
     n_splits = n_splits or -(-s_max // split)
     partials = np.zeros((n_splits, nh, d_c + 1), F32)
+    L = _od()
+    if L is not None and not debug_scores and split <= 4096:      # detdot.c: the same operations
+        L.od_mla_attend(ql_nope.ctypes.data, q_pe.ctypes.data, c_kv.ctypes.data, k_pe.ctypes.data, nh, d_c,
+                        q_pe.shape[1], int(step), F32(softmax_scale), int(split), int(n_splits),
+                        partials.ctypes.data)
+        return partials
     scores_all = np.zeros((nh, step + 1), F32) if debug_scores else None
     scale = F32(softmax_scale)
     for j in range(n_splits):
@@ -188,7 +196,7 @@ def mla_merge_uv(partials, W_uv, step, *, split=32, d_c=None):
     """attn [nh * d_v]: per head the merge, o rounded to BF16, then bf16(W_uv[h] o[h])
     (numpy_ref.py:168-174)."""
     o = bf16(merge_partials(partials, step, split=split, d_c=d_c))
-    W_uv = np.asarray(W_uv, F32)
+    W_uv = np.asarray(W_uv)
     attn = np.stack([dot_rows(W_uv[h], o[h]) for h in range(W_uv.shape[0])])
     return bf16(attn.reshape(-1))
 
@@ -297,7 +305,7 @@ def dense_mlp(h, W_gu, W_down, x_res, i_dense):
 
 def embed(W_embed, token):
     """x_res = W_embed[token] (the stock embedding task, fleet/graph_plan.py:416-418)."""
-    return np.asarray(W_embed[int(token)], F32).copy()
+    return vals(W_embed[int(token)]).copy()
 
 
 def lm_head_argmax(x_res, w_final_norm, W_lm, eps=1e-6):

@@ -55,3 +55,33 @@ class DeviceWeights:
         if key not in self.cache:
             self.cache[key] = np32(self.packed[name][e])
         return self.cache[key]
+
+
+def u16(t):
+    """A BF16 device tensor as its uint16 bit patterns on the host."""
+    return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+class DeviceWeightBits:
+    """The oracle's weight accessors over device tensors, as BF16 bit patterns (uint16 numpy, which
+    the oracle's row dots read directly). Tensors other than the experts are copied once; a routed
+    expert is copied on every use and only the always-selected (shared) experts are kept, so the host
+    holds a few GB while the oracle decodes the 31 GB model."""
+
+    def __init__(self, packed, keep_experts=()):
+        self.packed = packed
+        self.keep = set(keep_experts)
+        self.cache = {}
+
+    def get(self, name):
+        if name not in self.cache:
+            self.cache[name] = u16(self.packed[name])
+        return self.cache[name]
+
+    def get_expert(self, name, e):
+        if e not in self.keep:
+            return u16(self.packed[name][e])
+        key = (name, e)
+        if key not in self.cache:
+            self.cache[key] = u16(self.packed[name][e])
+        return self.cache[key]

@@ -171,3 +171,53 @@ def test_block_and_lane_sums():
     assert D.block_sum(v, vec=1) == tot
     assert abs(float(D.lane_sum(v[:70])) - float(v[:70].astype(np.float64).sum())) < 1e-5
     assert D.seq_sum(v[:5]) == np.float32(np.float32(np.float32(np.float32(v[0] + v[1]) + v[2]) + v[3]) + v[4])
+
+
+# ---- the C restatement of the hot loops (oracle/detdot.c) equals the numpy specification
+
+def _c_lib():
+    from oracle import detmath as D
+    L = D._od()
+    if L is None:
+        pytest.skip("oracle/libdetdot.so is not built (make -C oracle)")
+    return D, L
+
+
+@pytest.mark.parametrize("K", [64, 96, 128, 256, 512, 1024, 1408, 2048, 10944])
+def test_c_dot_rows_equals_numpy(K):
+    D, _ = _c_lib()
+    rng = np.random.default_rng(K)
+    W = D.bf16((rng.standard_normal((29, K)) * 0.02).astype(np.float32))
+    x = D.bf16(rng.standard_normal(K).astype(np.float32))
+    want = D.dot_rows_np(W, x).view(np.uint32)
+    assert np.array_equal(D.dot_rows(W, x).view(np.uint32), want)
+    assert np.array_equal(D.dot_rows(D.bf16_bits(W), x).view(np.uint32), want)
+
+
+def test_c_exp_log_equal_numpy():
+    D, L = _c_lib()
+    rng = np.random.default_rng(5)
+    xs = np.concatenate([(rng.standard_normal(4000) * 30).astype(np.float32),
+                         np.array([-87, -87.5, 88, 88.1, 0, -0.0, 1e-40, 1e-38, np.inf, -np.inf], np.float32)])
+    got = np.array([L.od_det_exp(float(v)) for v in xs], np.float32)
+    assert np.array_equal(got.view(np.uint32), D.det_exp(xs).view(np.uint32))
+    ys = np.concatenate([np.abs(xs), np.array([1e-42, 1e-39, 3.4e38], np.float32)])
+    got = np.array([L.od_det_log(float(v)) for v in ys], np.float32)
+    assert np.array_equal(got.view(np.uint32), D.det_log(ys).view(np.uint32))
+
+
+@pytest.mark.parametrize("nh,dc,dr,s,pos,split", [(16, 512, 64, 1100, 1050, 128), (4, 64, 16, 300, 250, 24),
+                                                  (16, 512, 64, 200, 63, 32)])
+def test_c_mla_attend_equals_numpy(nh, dc, dr, s, pos, split):
+    D, _ = _c_lib()
+    from oracle import numpy_ref as R
+    rng = np.random.default_rng(pos)
+    bf = lambda *sh: D.bf16(rng.standard_normal(sh).astype(np.float32))  # noqa: E731
+    args = (bf(nh, dc), bf(nh, dr), bf(s, dc), bf(s, dr), pos, 0.11)
+    got = R.mla_attend(*args, split=split)
+    saved, D._OD_LIB = D._OD_LIB, False
+    try:
+        want = R.mla_attend(*args, split=split)
+    finally:
+        D._OD_LIB = saved
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
