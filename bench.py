@@ -379,13 +379,13 @@ def cpu_baseline(packed, capture, meta, d, plan, budget_s, n_prompt=N_PROMPT):
 
 def roofline(d, ms_per_token, ctx, bw_peak, peak_kind, world=1):
     """Algorithmic HBM bytes of one GPU's launch per token over its time: with expert parallelism
-    rank 0 (the busiest) reads the replicated weights and ceil(TOPK / world) of the TOPK routed
-    slots' expert weights."""
-    from fleet.pack_weights import active_bytes_per_token, routed_bytes_per_token
+    rank 0 (the busiest) reads the replicated weights and the expert weights of ceil(N_SLOTS /
+    world) of the eight slots."""
+    from fleet.pack_weights import active_bytes_per_token, slot_bytes_per_token
     algo = active_bytes_per_token(d, ctx=ctx)
     if world > 1:
-        mine = -(-d.TOPK // world)
-        algo -= routed_bytes_per_token(d) * (d.TOPK - mine) // d.TOPK
+        mine = -(-d.N_SLOTS // world)
+        algo -= slot_bytes_per_token(d) * (d.N_SLOTS - mine)
     achieved = algo / (ms_per_token * 1e-3) / 1e9
     traffic = None
     f = ROOT / "profiles" / "decode_traffic.txt"
@@ -419,8 +419,8 @@ def run_ours(args):
             dist.all_gather_object(objs, obj)
             return objs
 
-        # expert parallelism by slot: rank r computes the routed slots s with s mod N = r; every
-        # rank holds every expert's weights and runs the rest of the graph
+        # expert parallelism by slot: rank r computes the slots s (six routed, two shared) with
+        # s mod N = r; every rank holds every expert's weights and runs the rest of the graph
         ep = EpGroup(rank, ws, local, D.N_SLOTS, D.H, args.layers - 1, all_gather)
     d, packed, capture, meta, mpk, host, plan, t_setup = build_model(args, device, args.layers, ep)
     stream = torch.cuda.Stream(device=device)
@@ -446,6 +446,12 @@ def run_ours(args):
     st = mpk.status()
     ids = ids_check(meta, args)
     if dist:
+        # every rank must have decoded the same tokens and hold the same final residual
+        n_dec = args.warmup + args.steps + E2E_STEPS
+        mine = (meta["tokens"][0, args.ctx:args.ctx + n_dec].tolist(),
+                int(host["x_res"].view(torch.int16).to(torch.int64).sum().item()), st["error"])
+        every = all_gather(mine)
+        ids = dict(ids or {}, ranks_agree=all(x == every[0] for x in every), ranks=ws)
         t = torch.tensor([ms, e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, e2e_ms = t.tolist()
@@ -476,8 +482,9 @@ def run_ours(args):
                                 if args.ctx == N_PROMPT else
                                 f"C4-shaped: the C1 model at {args.ctx}-token context, batch 1, 1 launch/token"),
                    "layers": args.layers, "ctx": [ctx0, ctx0 + args.steps - 1], "parallelism":
-                   f"expert parallel x{ws}: the 6 routed slots dealt round-robin over the GPUs, the rest "
-                   "replicated; per-token latency is the max over ranks" if ws > 1 else "1 GPU",
+                   f"expert parallel x{ws}: the 8 expert slots (6 routed, 2 shared) dealt round-robin over the "
+                   "GPUs, attention, router, layer 0 and head replicated; per-token latency is the max over ranks"
+                   if ws > 1 else "1 GPU",
                    "l2": "no flush: 4.9 GB read per step >> 126 MB L2", "routing": args.routing,
                    "tokens_per_s": round(1e3 / ms, 2)},
         "tokens_per_s": round(1e3 / ms, 2),

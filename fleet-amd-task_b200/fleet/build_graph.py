@@ -78,8 +78,8 @@ def moe_router_layer(mk, t, input, w_norm, w_gate, h, topk_w, routing, mask, log
 def gateup_layer(mk, t, input, weight, act, inter, groups, expert, norm, w_norm=None, mask=None, mid=None, h_out=None,
                  eps=G.RMS_EPS, static_ids=False, ep=None):
     """static_ids: the mask holds constant expert ids (the shared experts), so the weights stream
-    without waiting for a router. ep (rank, world): expert parallelism by slot, only the routed
-    slots s with s mod world = rank, spread over the tasks."""
+    without waiting for a router. ep (rank, world, slot0): expert parallelism by slot, only the
+    groups g whose slot slot0 + g has (slot0 + g) mod world = rank, spread over the tasks."""
     K = weight.shape[-1]
     estride = weight.shape[-2] * K if weight.dim() == 3 else 0
     nexp = weight.shape[0] if weight.dim() == 3 else 1
@@ -87,7 +87,7 @@ def gateup_layer(mk, t, input, weight, act, inter, groups, expert, norm, w_norm=
     ips = {0: K, 1: inter, 2: groups, 3: estride, 4: nexp}
     if ep is not None:
         flags |= mk.F_EP
-        ips.update({5: ep[0], 6: ep[1]})
+        ips.update({5: ep[0], 6: ep[1], 7: ep[2] if len(ep) > 2 else 0})
     u = mk.P["gu"]
     return mk.make_op(mk.OP_GATEUP, flags, {u["X"]: input, u["WNORM"]: w_norm, u["W"]: weight, u["MASK"]: mask,
                                             u["MID"]: mid, u["ACT"]: act, u["HOUT"]: h_out}, ips, {0: eps})
@@ -95,9 +95,9 @@ def gateup_layer(mk, t, input, weight, act, inter, groups, expert, norm, w_norm=
 
 def moe_w2_combine_layer(mk, t, input, weight, mask, topk_w, residual, output, out8=None, ep=None, peers=None,
                          topk=None, layer=0):
-    """ep (rank, world): expert parallelism by slot; the task computes its rank's routed slots and
-    the shared ones for its rows, exchanges the routed rows with the same task of every peer
-    (`peers`, fleet/ep.py) and combines all slots (out8 is then not written)."""
+    """ep (rank, world): expert parallelism by slot; the task computes its rank's slots (s mod world
+    = rank) for its rows, exchanges them with the same task of every peer (`peers`, fleet/ep.py)
+    and combines all slots (out8 is then not written)."""
     E, H, I = weight.shape
     assert residual.data_ptr() == output.data_ptr(), "the combine adds into x_res in place"
     n_slots = input.shape[0]

@@ -44,15 +44,16 @@ def float_bits(x: float) -> int:
     return struct.unpack("<i", struct.pack("<f", x))[0]
 
 
-EP_PEERS_WORDS = 36          # sizeof(MkEpPeers) / 4
+EP_PEERS_WORDS = 24          # sizeof(MkEpPeers) / 4
 
 
-def ep_slots(rank, world, topk):
-    """The routed slots rank `rank` of `world` computes under expert parallelism by slot: s mod
-    world = rank (every rank holds every expert's weights, so the six routed slots of a token
-    spread over the ranks whatever experts the router picks)."""
+def ep_slots(rank, world, n_slots):
+    """The slots rank `rank` of `world` computes under expert parallelism by slot: s mod world =
+    rank over all n_slots slots (the TOPK routed ones, then the shared ones). Every rank holds every
+    expert's weights, so a token's eight slots spread over the ranks whatever experts the router
+    picks: each rank gets ceil or floor of 8 / world."""
     assert 1 <= world and 0 <= rank < world, (rank, world)
-    return [s for s in range(topk) if s % world == rank]
+    return [s for s in range(n_slots) if s % world == rank]
 
 
 def partials_row(d_c):
@@ -206,9 +207,9 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
     """The operator chain for `layers` layers (+ the head). logit_bias: every router adds an
     injected FP32 bias [E] to its logits (the skewed/uniform routing of config 3). softmax_scale:
     default q_head_dim^-0.5 times the YaRN mscale^2 of the dims (0.1147213867929261 at REAL_DIMS).
-    ep (rank, world): expert parallelism by slot (fleet/ep.py): this rank's routed gate/up and down
-    projection cover the routed slots s with s mod world = rank; each down-projection task
-    exchanges its rows with the same task of every peer before it combines."""
+    ep (rank, world): expert parallelism by slot (fleet/ep.py): this rank's gate/up operators and
+    down projection cover the slots s (routed, then shared) with s mod world = rank; each
+    down-projection task exchanges its rows with the same task of every peer before it combines."""
     from fleet.capture import softmax_scale as yarn_softmax_scale
     d = dims
     scale = yarn_softmax_scale(d.D_N, d.D_R) if softmax_scale is None else softmax_scale
@@ -288,10 +289,11 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
                  scaling=ROUTED_SCALING, eps=RMS_EPS, **bias)
             # the shared experts (slots TOPK..) need no routing: they run beside the router, on
             # their own RMSNorm of x_res
+            ep_s = {} if ep is None else dict(ep=(ep[0], ep[1], d.TOPK))
             p.op("gateup_layer", f"L{l}.w13s", deps=(f"L{l}.o_proj",), beside=(f"L{l}.router",), input="x_res",
                  w_norm=f"w_norm2_{l}",
                  weight=f"W13_{l}", mask="mask_shared", mid=Rows("mid", d.TOPK), act=Rows("act8", d.TOPK),
-                 groups=d.N_SHARED, expert=True, static_ids=True, norm=True, eps=RMS_EPS, inter=d.I_MOE)
+                 groups=d.N_SHARED, expert=True, static_ids=True, norm=True, eps=RMS_EPS, inter=d.I_MOE, **ep_s)
             if ep is None:
                 p.op("gateup_layer", f"L{l}.w13r", deps=(f"L{l}.router",), input="h", weight=f"W13_{l}",
                      mask="mask", mid="mid", act="act8", groups=d.TOPK, expert=True, norm=False, inter=d.I_MOE)
@@ -300,7 +302,7 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
             else:
                 p.op("gateup_layer", f"L{l}.w13r", deps=(f"L{l}.router",), input="h", weight=f"W13_{l}",
                      mask="mask", mid="mid", act="act8", groups=d.TOPK, expert=True, norm=False, inter=d.I_MOE,
-                     ep=tuple(ep))
+                     ep=(ep[0], ep[1], 0))
                 p.op("moe_w2_combine_layer", f"L{l}.w2_combine", deps=(f"L{l}.w13r", f"L{l}.w13s"), input="act8",
                      weight=f"W2_{l}", mask="mask", topk_w="topk_w", residual="x_res", output="x_res",
                      ep=tuple(ep), peers="ep_peers", topk=d.TOPK, layer=l - 1)

@@ -73,13 +73,18 @@ enum MkOpType {
 #define MK_F_EXPERT (1 << 3)     /* GATEUP: groups are the routed slots of `mask` */
 #define MK_F_STATIC_IDS (1 << 4) /* GATEUP: `mask` holds constant expert ids (no wait for a router) */
 #define MK_F_EP (1 << 5)         /* GATEUP / W2_COMBINE: expert parallelism by slot over N ranks, each
-                                    holding every expert's weights: rank r computes the routed slots
-                                    s with s mod N = r (GATEUP spreads their pairs over its tasks;
-                                    the shared slots stay on every rank). W2_COMBINE task t computes
-                                    those slots and the shared ones for its rows, stores the routed
-                                    rows into every peer's exchange buffer, signals the peers'
-                                    task-t counters, waits for its own (every peer's task t), and
-                                    combines all slots */
+                                    holding every expert's weights: slot s (the TOPK routed slots,
+                                    then the shared ones) is computed by rank s mod N. GATEUP spreads
+                                    its rank's groups over its tasks (group g is slot SLOT0 + g).
+                                    W2_COMBINE task t computes its rank's slots for its rows, stores
+                                    them into every peer's exchange words, reads the other ranks'
+                                    slots from its own words as they arrive (each 64-bit word carries
+                                    its iteration tag) and combines all slots in slot order */
+#define MK_F_TC (1 << 6)         /* MLA_ATTEND: the tensor-core form (mma.sync BF16, FP32 accumulation):
+                                    one task per split for all 16 heads, cache rows streamed as TMA
+                                    boxes; DC 512, DR 64, 16 heads, head group 16. Its sums run in the
+                                    tensor cores' order, so its partials match the specified-order
+                                    form within rounding, not bit for bit */
 
 #define MK_MAX_PTRS 16
 #define MK_MAX_IPARAMS 16
@@ -120,23 +125,26 @@ enum { /* MK_OP_ROUTER */ MK_P_RT_X = 0, MK_P_RT_WNORM = 1, MK_P_RT_WGATE = 2, M
 enum { /* MK_OP_GATEUP */ MK_P_GU_X = 0, MK_P_GU_WNORM = 1, MK_P_GU_W = 2, MK_P_GU_MASK = 3,
        MK_P_GU_MID = 4, MK_P_GU_ACT = 5, MK_P_GU_HOUT = 6,
        MK_I_GU_K = 0, MK_I_GU_I = 1, MK_I_GU_GROUPS = 2, MK_I_GU_ESTRIDE = 3, MK_I_GU_NEXP = 4,
-       MK_I_GU_EPRANK = 5, MK_I_GU_EPWORLD = 6 };
+       MK_I_GU_EPRANK = 5, MK_I_GU_EPWORLD = 6, MK_I_GU_SLOT0 = 7 };
 enum { /* MK_OP_W2_COMBINE */ MK_P_W2_ACT = 0, MK_P_W2_W = 1, MK_P_W2_MASK = 2, MK_P_W2_TOPKW = 3,
        MK_P_W2_XRES = 4, MK_P_W2_OUT8 = 5,
        MK_P_W2_PEERS = 6,   /* MK_F_EP: device MkEpPeers */
        MK_I_W2_H = 0, MK_I_W2_I = 1, MK_I_W2_SLOTS = 2, MK_I_W2_ESTRIDE = 3, MK_I_W2_NEXP = 4,
-       MK_I_W2_TOPK = 5, MK_I_W2_EPRANK = 6, MK_I_W2_EPWORLD = 7, MK_I_W2_LAYER = 8 };
-/* Expert parallelism: where each rank's exchange buffers are, as this rank maps them (peer
-   pointers opened with mk_ep_ipc_open). out8[r] is rank r's [2][slots][H] BF16 exchange buffer
-   (halves by MoE-layer parity) and counter[r] its [layers][MK_EP_MAX_TASKS] arrival counters
-   (32-bit, monotonic; a peer's down-projection task t adds 1 per iteration). */
+       MK_I_W2_TOPK = 5, MK_I_W2_EPRANK = 6, MK_I_W2_EPWORLD = 7,
+       MK_I_W2_LAYER = 8 /* MK_F_EP: the exchange layer, 0 <= layer < MkEpPeers.n_layers */ };
+/* Expert parallelism: where each rank's exchange words are, as this rank maps them (peer pointers
+   opened with mk_ep_ipc_open). xch[r] is rank r's [2][n_layers][n_slots][hidden / 2] array of
+   64-bit words: the low half holds two BF16 outputs (rows 2k, 2k + 1 of one slot), the high half
+   the iteration tag that wrote them (the handle's exchange iteration, 1-based; halves alternate by
+   its parity). A sender stores whole words (one 64-bit store each), so a reader that sees the tag
+   it expects also sees the data: no fence and no separate counter. */
 #define MK_EP_MAX_RANKS 8
 #define MK_EP_MAX_TASKS 256
 typedef struct MkEpPeers {
-  void* out8[MK_EP_MAX_RANKS];
-  uint32_t* counter[MK_EP_MAX_RANKS];
+  uint64_t* xch[MK_EP_MAX_RANKS];
   int32_t nranks, rank;
-  int32_t reserved[2];
+  int32_t n_layers, n_slots, hidden;   /* the geometry the buffers were allocated for */
+  int32_t reserved[3];
 } MkEpPeers;
 enum { /* MK_OP_STREAM */ MK_P_ST_W = 0, MK_P_ST_OUT = 1, MK_I_ST_ROWS = 0, MK_I_ST_K = 1 };
 
@@ -196,7 +204,10 @@ int mk_reset(MkHandle* h);
 int mk_trace(MkHandle* h, MkTraceRecord* out, int64_t cap, int64_t* n);
 /* Expert parallelism buffers (no counterpart in the reference, which exchanged through NCCL):
    device memory that peer processes can map (cudaMalloc, zeroed), its 64-byte IPC handle, and a
-   peer's buffer opened in this process (peer access enabled lazily); close and free release them. */
+   peer's buffer opened in this process (peer access enabled lazily); close and free release them.
+   Every rank of a group must launch the same iteration counts: the exchange tags count the
+   handle's iterations since mk_finalize (a failed launch consumes its iterations too, and
+   mk_reset keeps the count), so the ranks' tags stay equal. */
 int mk_ep_alloc(int32_t device, size_t bytes, void** dev_ptr);
 int mk_ep_free(void* dev_ptr);
 int mk_ep_ipc_handle(void* dev_ptr, void* handle64);

@@ -1,7 +1,9 @@
-"""One rank of an expert-parallel decode run (launched by tests/test_gpu_ep.py and by bench.py's
-multi-GPU leg through torch.distributed.run): builds the same small model on every rank with
-fleet.ep.EpGroup, runs greedy iterations in one launch, and writes this rank's tokens and final
-residual to <out>/rank<r>.npz. Exit code 0 on success."""
+"""One rank of an expert-parallel decode run (launched by tests/test_gpu_ep.py through
+torch.distributed.run): builds the same small model on every rank with fleet.ep.EpGroup, runs
+greedy iterations in one launch, then a second launch of more iterations (the exchange tags carry
+over launches), and writes this rank's tokens, route log and final residual to <out>/rank<r>.npz.
+An odd MoE-layer count (the default: 4 layers, 3 MoE layers) checks that the exchange words of
+one token's last MoE layer and the next token's first are not confused. Exit code 0 on success."""
 import argparse
 import os
 import sys
@@ -34,7 +36,7 @@ def build(dims, layers, iters, n_past, seed, ep, device):
     return mpk, host, meta, plan
 
 
-def run(out, layers=4, iters=4, n_past=40, seed=0):
+def run(out, layers=4, iters=4, n_past=40, seed=0, second=3):
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -50,16 +52,18 @@ def run(out, layers=4, iters=4, n_past=40, seed=0):
 
     dims = small_dims()
     ep = EpGroup(rank, world, local, dims.N_SLOTS, dims.H, dims.L - 1, all_gather)
-    mpk, host, meta, plan = build(dims, layers, iters, n_past, seed, ep, f"cuda:{local}")
+    mpk, host, meta, plan = build(dims, layers, iters + second, n_past, seed, ep, f"cuda:{local}")
     mpk.compile()
     dist.barrier()
-    meta["step"].fill_(n_past - 1)
-    mpk()
+    mpk.step = n_past - 1
+    mpk.launch(iters)
+    mpk.launch(second)
     torch.cuda.synchronize()
     st = mpk.status(raise_on_error=False)
     tokens = meta["tokens"][0].cpu().numpy()
     x_res = host["x_res"].view(torch.int16).cpu().numpy()
-    np.savez(Path(out) / f"rank{rank}.npz", tokens=tokens, x_res=x_res, error=st["error"])
+    np.savez(Path(out) / f"rank{rank}.npz", tokens=tokens, x_res=x_res, error=st["error"],
+             route_log=host["route_log"].cpu().numpy())
     dist.barrier()          # every peer is done writing into this rank's buffers
     mpk.kernel.close()
     ep.close()
