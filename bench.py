@@ -52,6 +52,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--routing", default="natural", choices=["natural", "uniform", "zipf"],
                     help="config 3's injected router logits (seed 4): uniform, or Zipf s=1.2 over the experts")
+    ap.add_argument("--attend", default="exact", choices=["exact", "tc"],
+                    help="MLA attention form: the bit-exact FP32 CUDA-core tasks, or the tensor-core tasks")
+    ap.add_argument("--split", type=int, default=None, help="cache rows per attention split (default: the plan's)")
+    ap.add_argument("--tc-parts", type=int, default=1, help="tensor-core attention: latent-column parts per split")
     ap.add_argument("--trace", action="store_true",
                     help="record per-task %%globaltimer stamps and print a per-operator breakdown of the last "
                          "token to stderr (the timed numbers then include the stamping)")
@@ -196,8 +200,10 @@ def build_model(args, device, layers, ep=None):
     if routing != "natural":
         from fleet.capture import router_biases
         capture.update(router_biases(d, layers, routing, seed=4, device=device))
+    extra = {} if args.split is None else dict(split=args.split)
     mpk, host, plan = B.build(packed, capture, meta, dims=d, s_max=s_max, layers=layers, head=True,
-                              trace=args.trace, ep=ep, logit_bias=routing != "natural")
+                              trace=args.trace, ep=ep, logit_bias=routing != "natural",
+                              attend_tc=args.attend == "tc", tc_parts=args.tc_parts, **extra)
     mpk.compile()
     torch.cuda.synchronize()
     return d, packed, capture, meta, mpk, host, plan, time.time() - t0
@@ -486,6 +492,9 @@ def run_ours(args):
                    "GPUs, attention, router, layer 0 and head replicated; per-token latency is the max over ranks"
                    if ws > 1 else "1 GPU",
                    "l2": "no flush: 4.9 GB read per step >> 126 MB L2", "routing": args.routing,
+                   "attention": ("tensor cores (mma.sync BF16, FP32 accumulation)" if args.attend == "tc" else
+                                 "FP32 CUDA cores, specified summation order (bit-exact)"),
+                   "split": plan.split, "tc_parts": args.tc_parts if args.attend == "tc" else None,
                    "tokens_per_s": round(1e3 / ms, 2)},
         "tokens_per_s": round(1e3 / ms, 2),
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms/token", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,

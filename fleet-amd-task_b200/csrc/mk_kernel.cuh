@@ -30,7 +30,8 @@ constexpr int TC_P_OFF = TC_Q_OFF + 16 * TC_QSTRIDE;
 constexpr int TC_OWN_OFF = TC_P_OFF + 16 * TC_PSTRIDE;
 constexpr int TC_ZERO_OFF = TC_OWN_OFF + 576 * 2;
 constexpr int TC_RED_OFF = TC_ZERO_OFF + 16;
-constexpr int TC_SCRATCH_END = TC_RED_OFF + 2 * NUM_CONSUMER_WARPS * 16 * 4;
+constexpr int TC_HALF_OFF = TC_RED_OFF + 2 * NUM_CONSUMER_WARPS * 16 * 4;   // [4 pairs][32 lanes][8] partial scores
+constexpr int TC_SCRATCH_END = TC_HALF_OFF + 4 * 32 * 8 * 4;
 static_assert(TC_SCRATCH_END <= SCRATCH_BYTES, "tensor-core attention scratch");
 static_assert(TC_STAGE_TX <= STAGE_BYTES && TC_CHUNK_STAGES < NSTAGES, "tensor-core attention stages");
 
@@ -230,6 +231,14 @@ __device__ void op_embed(const KernelParams& P, Smem& sm, const OpDev& od, const
   const uint4* src = reinterpret_cast<const uint4*>(P_<const uint16_t>(od, MK_P_EMB_W) + tok * H);
   uint4* dst = reinterpret_cast<uint4*>(P_<uint16_t>(od, MK_P_EMB_OUT));
   for (int i = c.tid; i < (int)(H / 8); i += NUM_CONSUMERS) dst[i] = __ldg(src + i);
+}
+
+// ---- copy (the debug residual snapshot) -------------------------------------------------------
+__device__ void op_copy(const OpDev& od, Cons& c) {
+  const int64_t n = I_(od, MK_I_CP_N);
+  const uint4* src = reinterpret_cast<const uint4*>(P_<const uint16_t>(od, MK_P_CP_SRC));
+  uint4* dst = reinterpret_cast<uint4*>(P_<uint16_t>(od, MK_P_CP_DST));
+  for (int64_t i = c.tid; i < n / 8; i += NUM_CONSUMERS) dst[i] = ldcg16(src + i);
 }
 
 // ---- the row-dot engine ---------------------------------------------------------------------
@@ -612,6 +621,8 @@ __device__ void attend_body(const KernelParams& P, Smem& sm, const OpDev& od, co
     }
   }
   consumer_sync();
+  if (float* dbg = P_<float>(od, MK_P_ATT_SCORES))   // debug: the scaled scores of this head's rows
+    for (int r = c.tid; r < rows; r += NUM_CONSUMERS) dbg[(size_t)h * I_(od, MK_I_ATT_SMAX) + a.lo + r] = sc[r];
   // softmax: every warp finds m; thread r computes p_r; warp 0 adds l in the lane order
   float mx = -__int_as_float(0x7F800000);
   for (int r = c.lane; r < rows; r += 32) mx = fmaxf(mx, sc[r]);
@@ -809,6 +820,10 @@ __device__ __forceinline__ void attend_pairs(const KernelParams& P, Smem& sm, co
       }
     }
     consumer_sync();
+    if (float* dbg = P_<float>(od, MK_P_ATT_SCORES))   // debug: the scaled scores of both heads' rows
+      for (int u = c.tid; u < 2 * rows; u += NUM_CONSUMERS)
+        dbg[(size_t)(u < rows ? hA : hB) * I_(od, MK_I_ATT_SMAX) + a.lo + (u < rows ? u : u - rows)] =
+            u < rows ? H0.sc[u] : H1.sc[u - rows];
     // softmax: every warp finds both maxima; thread u computes p of row u mod rows of head u / rows
     float ma = -__int_as_float(0x7F800000), mb = ma;
     for (int r = c.lane; r < rows; r += 32) {
@@ -922,17 +937,24 @@ struct TcRows {    // where a chunk's rows are: nt streamed rows in ring stages 
   }
 };
 
-__device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const OpDev& od, const TaskDev& t, const Iter& itx,
-                          Cons& c) {
+// Out of line: its own register allocation, so the inlined operators keep theirs. The lane
+// indices are copied into registers at entry (through the caller's reference they would be
+// reloaded from local memory, whose lines miss the small L1 beside the shared-memory carveout).
+__device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const OpDev& od, const TaskDev& t,
+                                      const Iter itx, Cons& c) {
+  const int warp = c.warp, lane = c.lane, tid = c.tid;
   constexpr int DC = 512, DR = 64, NH = 16;
   const int prow = (int)I_(od, MK_I_ATT_PROW), j = t.b;
+  // latent-column part q of QN: this task's P.V covers columns [q * CW, q * CW + CW)
+  const int QN = (int)I_(od, MK_I_ATT_CPARTS), q = t.a, CW = DC / QN, npairs = CW / 16;
   const float scale = (float)od.op.fp[0];
   float* partials = P_<float>(od, MK_P_ATT_PARTIALS);
   const AttSplit a = att_split(od, t, itx.pos);
   const float NEG_INF = -__int_as_float(0x7F800000);
   if (a.hi <= a.lo) {   // no live row at this position: o = 0, lse = -inf
-    for (int i = c.tid; i < NH * DC; i += NUM_CONSUMERS) partials[((size_t)j * NH + i / DC) * prow + i % DC] = 0.0f;
-    if (c.tid < NH) partials[((size_t)j * NH + c.tid) * prow + DC] = NEG_INF;
+    for (int i = tid; i < NH * CW; i += NUM_CONSUMERS)
+      partials[((size_t)j * NH + i / CW) * prow + q * CW + i % CW] = 0.0f;
+    if (q == 0 && tid < NH) partials[((size_t)j * NH + tid) * prow + DC] = NEG_INF;
     return;
   }
   const int rows = a.hi - a.lo, nstr = a.n_str;
@@ -942,7 +964,7 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
   {
     const uint16_t* qln = P_<const uint16_t>(od, MK_P_ATT_QLNOPE);
     const uint16_t* qpe = P_<const uint16_t>(od, MK_P_ATT_QPE);
-    for (int i = c.tid; i < NH * 72; i += NUM_CONSUMERS) {
+    for (int i = tid; i < NH * 72; i += NUM_CONSUMERS) {
       const int h = i / 72, q8 = i - h * 72;
       const uint4 v = q8 < 64 ? ldcg16(qln + (size_t)h * DC + q8 * 8) : ldcg16(qpe + (size_t)h * DR + (q8 - 64) * 8);
       *reinterpret_cast<uint4*>(scr + TC_Q_OFF + h * TC_QSTRIDE + q8 * 16) = v;
@@ -950,13 +972,13 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
     if (a.has_pos) {
       const uint16_t* ck = P_<const uint16_t>(od, MK_P_ATT_CKV) + (size_t)itx.pos * DC;
       const uint16_t* kp = P_<const uint16_t>(od, MK_P_ATT_KPE) + (size_t)itx.pos * DR;
-      for (int i = c.tid; i < 72; i += NUM_CONSUMERS)
+      for (int i = tid; i < 72; i += NUM_CONSUMERS)
         *reinterpret_cast<uint4*>(scr + TC_OWN_OFF + i * 16) = i < 64 ? ldcg16(ck + i * 8) : ldcg16(kp + (i - 64) * 8);
     }
-    if (c.tid == 0) *reinterpret_cast<uint4*>(scr + TC_ZERO_OFF) = make_uint4(0u, 0u, 0u, 0u);
+    if (tid == 0) *reinterpret_cast<uint4*>(scr + TC_ZERO_OFF) = make_uint4(0u, 0u, 0u, 0u);
   }
   float* red = reinterpret_cast<float*>(scr + TC_RED_OFF);   // [2][8 warps][16 heads]
-  const int g = c.lane >> 2, tig = c.lane & 3;
+  const int g = lane >> 2, tig = lane & 3;
   // running softmax statistics of heads g and g + 8 (every thread of a group keeps the same)
   float m_g = NEG_INF, m_g8 = NEG_INF, l_g = 0.0f, l_g8 = 0.0f;
   float o[8][4];
@@ -977,25 +999,57 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
     for (int s = 0; s < ns; ++s) acquire_stage(P, sm, c, (uint32_t)t.op, (uint32_t)t.idx);
     consumer_sync();   // Q, the own row and the zero chunk are visible (first chunk)
     if (!marked) { mark_body(sm, c); marked = true; }
-    // ---- S = Q K^T: warp w takes the 16-row pairs w, w + 8, ... of the chunk
+    // ---- S = Q K^T over 16-row pairs of the chunk: with at most four pairs, two warps share a pair
+    // (the first and second half of the 36 k-steps, added through shared memory), else one warp
+    // per pair; each warp keeps two accumulator sets (even and odd k-steps) so two mma chains
+    // overlap
     const int pairs = (R + 15) / 16;
+    const bool split_k = pairs <= 4;
+    const int jp = split_k ? (warp >> 1) : warp, kh = split_k ? (warp & 1) : 0;
+    const int k0 = split_k ? 18 * kh : 0, k1 = split_k ? k0 + 18 : 36;
     float mx_g = NEG_INF, mx_g8 = NEG_INF;
     float acc[2][4];
-    const int jp = c.warp;
-    const bool has_pair = jp < pairs;
-    if (has_pair) {
+    const bool in_pair = jp < pairs;
+    const bool has_pair = in_pair && kh == 0;     // this warp owns the pair's finished scores
+    if (in_pair) {
+      float accb[2][4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[0][i] = acc[1][i] = 0.0f;
-      const int qh = (c.lane & 7) + 8 * ((c.lane >> 3) & 1), qk = 8 * (c.lane >> 4);
-      const int br = 16 * jp + (c.lane & 7) + 8 * (c.lane >> 4), bk = 8 * ((c.lane >> 3) & 1);
+      for (int i = 0; i < 4; ++i) acc[0][i] = acc[1][i] = accb[0][i] = accb[1][i] = 0.0f;
+      const int qh = (lane & 7) + 8 * ((lane >> 3) & 1), qk = 8 * (lane >> 4);
+      const int br = 16 * jp + (lane & 7) + 8 * (lane >> 4), bk = 8 * ((lane >> 3) & 1);
       const uint32_t qa = qbase + (uint32_t)(qh * TC_QSTRIDE + qk * 2);
-#pragma unroll 4
-      for (int kk = 0; kk < 36; ++kk) {
-        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+#pragma unroll 2
+      for (int kk = k0; kk < k1; kk += 2) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3, e0, e1, e2, e3, f0, f1, f2, f3;
         ldsm_x4(qa + (uint32_t)kk * 32u, a0, a1, a2, a3);
         ldsm_x4(tr.at(br, 16 * kk + bk), b0, b1, b2, b3);
+        ldsm_x4(qa + (uint32_t)(kk + 1) * 32u, e0, e1, e2, e3);
+        ldsm_x4(tr.at(br, 16 * (kk + 1) + bk), f0, f1, f2, f3);
         mma_bf16_16816(acc[0], a0, a1, a2, a3, b0, b1);
         mma_bf16_16816(acc[1], a0, a1, a2, a3, b2, b3);
+        mma_bf16_16816(accb[0], e0, e1, e2, e3, f0, f1);
+        mma_bf16_16816(accb[1], e0, e1, e2, e3, f2, f3);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[0][i] = __fadd_rn(acc[0][i], accb[0][i]);
+        acc[1][i] = __fadd_rn(acc[1][i], accb[1][i]);
+      }
+      if (split_k && kh == 1) {
+        float* hp = reinterpret_cast<float*>(scr + TC_HALF_OFF) + (jp * 32 + lane) * 8;
+        *reinterpret_cast<float4*>(hp) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+        *reinterpret_cast<float4*>(hp + 4) = make_float4(acc[1][0], acc[1][1], acc[1][2], acc[1][3]);
+      }
+    }
+    if (split_k) consumer_sync();   // the second halves' partial scores
+    if (has_pair) {
+      if (split_k) {
+        const float* hp = reinterpret_cast<const float*>(scr + TC_HALF_OFF) + (jp * 32 + lane) * 8;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[0][i] = __fadd_rn(acc[0][i], hp[i]);
+          acc[1][i] = __fadd_rn(acc[1][i], hp[4 + i]);
+        }
       }
       // scale, mask rows past the chunk, running maxima of heads g and g + 8
 #pragma unroll
@@ -1008,12 +1062,22 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
         mx_g = fmaxf(mx_g, fmaxf(acc[h][0], acc[h][1]));
         mx_g8 = fmaxf(mx_g8, fmaxf(acc[h][2], acc[h][3]));
       }
+      if (float* dbg = P_<float>(od, MK_P_ATT_SCORES)) {   // debug: the scaled scores of live rows
+        const int64_t smax = I_(od, MK_I_ATT_SMAX);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int r = 16 * jp + 8 * h + 2 * tig + (e & 1);
+            if (r < R) dbg[(size_t)(e < 2 ? g : g + 8) * smax + a.lo + c0 + r] = acc[h][e];
+          }
+      }
     }
     mx_g = fmaxf(mx_g, __shfl_xor_sync(0xffffffffu, mx_g, 1));
     mx_g = fmaxf(mx_g, __shfl_xor_sync(0xffffffffu, mx_g, 2));
     mx_g8 = fmaxf(mx_g8, __shfl_xor_sync(0xffffffffu, mx_g8, 1));
     mx_g8 = fmaxf(mx_g8, __shfl_xor_sync(0xffffffffu, mx_g8, 2));
-    if (tig == 0) { red[c.warp * 16 + g] = mx_g; red[c.warp * 16 + g + 8] = mx_g8; }
+    if (tig == 0) { red[warp * 16 + g] = mx_g; red[warp * 16 + g + 8] = mx_g8; }
     consumer_sync();
     float cm_g = NEG_INF, cm_g8 = NEG_INF;
 #pragma unroll
@@ -1044,8 +1108,8 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
     ls_g8 = __fadd_rn(ls_g8, __shfl_xor_sync(0xffffffffu, ls_g8, 1));
     ls_g8 = __fadd_rn(ls_g8, __shfl_xor_sync(0xffffffffu, ls_g8, 2));
     if (tig == 0) {
-      red[NUM_CONSUMER_WARPS * 16 + c.warp * 16 + g] = has_pair ? ls_g : 0.0f;
-      red[NUM_CONSUMER_WARPS * 16 + c.warp * 16 + g + 8] = has_pair ? ls_g8 : 0.0f;
+      red[NUM_CONSUMER_WARPS * 16 + warp * 16 + g] = has_pair ? ls_g : 0.0f;
+      red[NUM_CONSUMER_WARPS * 16 + warp * 16 + g + 8] = has_pair ? ls_g8 : 0.0f;
     }
     consumer_sync();   // P and the sums are complete
     float cs_g = 0.0f, cs_g8 = 0.0f;
@@ -1058,7 +1122,7 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
     l_g8 = __fadd_rn(__fmul_rn(l_g8, al_g8), cs_g8);
     m_g = mn_g;
     m_g8 = mn_g8;
-    // ---- O = O alpha + P V: warp w takes latent columns [64 w, 64 w + 64), eight n-tiles
+    // ---- O = O alpha + P V: the part's 16-column pairs w, w + 8, ... (at most four per warp)
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
       o[n][0] = __fmul_rn(o[n][0], al_g);
@@ -1067,17 +1131,20 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
       o[n][3] = __fmul_rn(o[n][3], al_g8);
     }
     {
-      const int ph = (c.lane & 7) + 8 * ((c.lane >> 3) & 1), pk = 8 * (c.lane >> 4);
-      const int vr = (c.lane & 7) + 8 * ((c.lane >> 3) & 1), vc = 64 * c.warp + 8 * (c.lane >> 4);
+      const int ph = (lane & 7) + 8 * ((lane >> 3) & 1), pk = 8 * (lane >> 4);
+      const int vr = (lane & 7) + 8 * ((lane >> 3) & 1), vc = q * CW + 8 * (lane >> 4);
       for (int kk = 0; kk < pairs; ++kk) {
         uint32_t a0, a1, a2, a3;
         ldsm_x4(pbase + (uint32_t)(ph * TC_PSTRIDE + (16 * kk + pk) * 2), a0, a1, a2, a3);
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(tr.at(16 * kk + vr, vc + 16 * np), b0, b1, b2, b3);
-          mma_bf16_16816(o[2 * np], a0, a1, a2, a3, b0, b1);
-          mma_bf16_16816(o[2 * np + 1], a0, a1, a2, a3, b2, b3);
+        for (int i = 0; i < 4; ++i) {
+          const int pi = warp + 8 * i;
+          if (pi < npairs) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(tr.at(16 * kk + vr, vc + 16 * pi), b0, b1, b2, b3);
+            mma_bf16_16816(o[2 * i], a0, a1, a2, a3, b0, b1);
+            mma_bf16_16816(o[2 * i + 1], a0, a1, a2, a3, b2, b3);
+          }
         }
       }
     }
@@ -1085,17 +1152,23 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
     for (int s = 0; s < ns; ++s) release_stage(sm, c);
   }
   mark_stages(sm, c);
-  // o = O / l and lse = m + log l into the split's partial rows
-  const float il_g = l_g, il_g8 = l_g8;
+  // o = O / l (one reciprocal per head) and lse = m + log l into the split's partial rows
+  const float il_g = __fdiv_rn(1.0f, l_g), il_g8 = __fdiv_rn(1.0f, l_g8);
   float* out_g = partials + ((size_t)j * NH + g) * prow;
   float* out_g8 = partials + ((size_t)j * NH + g + 8) * prow;
 #pragma unroll
-  for (int n = 0; n < 8; ++n) {
-    const int col = 64 * c.warp + 8 * n + 2 * tig;
-    *reinterpret_cast<float2*>(out_g + col) = make_float2(__fdiv_rn(o[n][0], il_g), __fdiv_rn(o[n][1], il_g));
-    *reinterpret_cast<float2*>(out_g8 + col) = make_float2(__fdiv_rn(o[n][2], il_g8), __fdiv_rn(o[n][3], il_g8));
+  for (int i = 0; i < 4; ++i) {
+    const int pi = warp + 8 * i;
+    if (pi < npairs) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int n = 2 * i + h, col = q * CW + 16 * pi + 8 * h + 2 * tig;
+        *reinterpret_cast<float2*>(out_g + col) = make_float2(__fmul_rn(o[n][0], il_g), __fmul_rn(o[n][1], il_g));
+        *reinterpret_cast<float2*>(out_g8 + col) = make_float2(__fmul_rn(o[n][2], il_g8), __fmul_rn(o[n][3], il_g8));
+      }
+    }
   }
-  if (c.warp == 0 && tig == 0) {
+  if (q == 0 && warp == 0 && tig == 0) {
     out_g[DC] = __fadd_rn(m_g, det_log(l_g));
     out_g8[DC] = __fadd_rn(m_g8, det_log(l_g8));
   }
@@ -1498,7 +1571,12 @@ __device__ __forceinline__ void by_parts(int K, F&& f) {
   if (parts_of(K) == 8) f(PartsTag<8>{});   // the model's K (2,048 and 1,408): unrolled
   else f(PartsTag<0>{});                    // every other K: run-time part count
 }
-template <bool LONGCTX>
+// Kernel variants: KV_SHORT (the exact attention, one head per task), KV_LONG (adds the exact
+// attention's two-heads-at-a-time form, used by head groups > 1 at long context), KV_TC (the
+// tensor-core attention instead of both). A plan's launches use the one variant that has its
+// operators, so the other forms' code does not sit in the hot kernel.
+enum { KV_SHORT = 0, KV_LONG = 1, KV_TC = 2 };
+template <int KV>
 __device__ void run_task(const KernelParams& P, Smem& sm, const OpDev& od, const TaskDev& t, const Iter& itx,
                          Cons& c) {
   switch (od.op.type) {
@@ -1511,12 +1589,14 @@ __device__ void run_task(const KernelParams& P, Smem& sm, const OpDev& od, const
     }
     case MK_OP_MLA_PREP: op_prep(P, sm, od, t, itx, c); break;
     case MK_OP_MLA_ATTEND: {
-      if (od.op.flags & MK_F_TC) {
-        attend_tc(P, sm, od, t, itx, c);
-        break;
+      if constexpr (KV == KV_TC) {
+        if (od.op.flags & MK_F_TC) {
+          attend_tc(P, sm, od, t, itx, c);
+          break;
+        }
       }
       if (I_(od, MK_I_ATT_DC) == 512 && I_(od, MK_I_ATT_DR) == 64) {
-        if constexpr (LONGCTX) {
+        if constexpr (KV == KV_LONG) {
           if ((I_(od, MK_I_ATT_HGROUP) & 1) == 0) {
             attend_pairs(P, sm, od, t, itx, c);
             break;
@@ -1544,6 +1624,7 @@ __device__ void run_task(const KernelParams& P, Smem& sm, const OpDev& od, const
       break;
     }
     case MK_OP_STREAM: op_stream(P, sm, od, t, itx, c); break;
+    case MK_OP_COPY: op_copy(od, c); break;
     default: break;
   }
 }
@@ -1560,7 +1641,7 @@ __device__ __forceinline__ void prefetch_task(const KernelParams& P, Smem& sm, u
                reinterpret_cast<const uint4*>(P.ctask + k) + (tid - OPDEV_CHUNKS));
 }
 
-template <bool LONGCTX>
+template <int KV>
 __device__ void consumer_main(const KernelParams& P, Smem& sm) {
   Cons c;
   c.c_it = 0u;
@@ -1607,7 +1688,7 @@ __device__ void consumer_main(const KernelParams& P, Smem& sm) {
       if (!sm.bcast[0]) goto done;
       {
         const Iter itx{it, P.step + 1 + it, P.gen0 + (uint32_t)it};
-        run_task<LONGCTX>(P, sm, sm.od_buf[slot], sm.ct_buf[slot].t, itx, c);
+        run_task<KV>(P, sm, sm.od_buf[slot], sm.ct_buf[slot].t, itx, c);
       }
       cp_async_wait_all();
       consumer_sync();
@@ -1636,10 +1717,8 @@ done:
   if (c.tid == 0 && *(volatile uint32_t*)&sm.cta_abort) atomicAdd(&P.status->aborted_ctas, 1u);
 }
 
-// Two instantiations: LONGCTX adds the two-heads-at-a-time attention (head groups > 1, which the
-// plan uses at long context only); the host launches it only when an attention operator has such
-// a group, so the 1K-context kernel carries none of that code.
-template <bool LONGCTX>
+// One instantiation per kernel variant (KV_SHORT, KV_LONG, KV_TC; see run_task).
+template <int KV>
 __global__ void __launch_bounds__(NUM_THREADS, 1) mk_persistent_kernel(const KernelParams P) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -1659,7 +1738,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) mk_persistent_kernel(const Ker
     if (threadIdx.x == NUM_CONSUMERS) producer_main(sm.kp, sm);
     return;
   }
-  consumer_main<LONGCTX>(sm.kp, sm);
+  consumer_main<KV>(sm.kp, sm);
 }
 
 }  // namespace mk

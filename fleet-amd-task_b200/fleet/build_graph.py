@@ -49,12 +49,20 @@ def mla_prep_layer(mk, t, qkva, w_kv_norm, w_ukT, cos, sin, c_kv, k_pe, ql_nope,
                       {0: nh, 1: d_n, 2: d_r, 3: d_c, 4: c_kv.shape[0]}, {0: eps})
 
 
-def mla_attend_layer(mk, t, ql_nope, q_pe, c_kv, k_pe, partials, softmax_scale, split, n_splits, head_group):
+def mla_attend_layer(mk, t, ql_nope, q_pe, c_kv, k_pe, partials, softmax_scale, split, n_splits, head_group,
+                     tc=False, scores=None, col_parts=1):
+    """tc: the tensor-core form (one task per split for all heads; head_group must be the head
+    count), else the FP32 CUDA-core form in the specified summation orders (bit-exact).
+    scores: optional [nh, s_max] FP32 output of the scaled scores (the reference's debug_scores,
+    boundary B5). col_parts (tc): latent-column parts per split, one task each (1, 2, 4 or 8)."""
     nh, d_c = ql_nope.shape
     assert partials.shape == (n_splits, nh, G.partials_row(d_c)), partials.shape
-    return mk.make_op(mk.OP_MLA_ATTEND, 0, dict(enumerate([ql_nope, q_pe, c_kv, k_pe, partials])),
+    assert not tc or head_group == nh, "the tensor-core attention takes all heads of a split in one task"
+    assert scores is None or tuple(scores.shape) == (nh, c_kv.shape[0]), "scores: [heads, s_max]"
+    return mk.make_op(mk.OP_MLA_ATTEND, mk.F_TC if tc else 0,
+                      dict(enumerate([ql_nope, q_pe, c_kv, k_pe, partials, scores])),
                       {0: nh, 1: d_c, 2: k_pe.shape[1], 3: c_kv.shape[0], 4: split, 5: head_group, 6: n_splits,
-                       7: partials.shape[2]}, {0: softmax_scale})
+                       7: partials.shape[2], 8: col_parts}, {0: softmax_scale})
 
 
 def mla_merge_uv_layer(mk, t, partials, w_uv, output, split, n_splits):
@@ -113,6 +121,12 @@ def moe_w2_combine_layer(mk, t, input, weight, mask, topk_w, residual, output, o
 
 
 
+def copy_layer(mk, t, input, output):
+    """output = input (the debug per-layer residual snapshot; the reference's copy_layer)."""
+    assert input.numel() == output.numel(), (input.shape, output.shape)
+    return mk.make_op(mk.OP_COPY, 0, {0: input, 1: output}, {0: input.numel()})
+
+
 def stream_layer(mk, t, weight, dummy, dummy_in=None):
     return mk.make_op(mk.OP_STREAM, 0, {0: weight, 1: dummy}, {0: weight.shape[0], 1: weight.shape[1]})
 
@@ -121,7 +135,7 @@ NEW_LAYERS = {
     "embed_layer": embed_layer, "linear_gemv_layer": linear_gemv_layer, "mla_prep_layer": mla_prep_layer,
     "mla_attend_layer": mla_attend_layer, "mla_merge_uv_layer": mla_merge_uv_layer,
     "moe_router_layer": moe_router_layer, "gateup_layer": gateup_layer,
-    "moe_w2_combine_layer": moe_w2_combine_layer, "stream_layer": stream_layer,
+    "moe_w2_combine_layer": moe_w2_combine_layer, "stream_layer": stream_layer, "copy_layer": copy_layer,
 }
 
 
@@ -129,16 +143,35 @@ NEW_LAYERS = {
 # driving the plan
 
 
-def new_workspace(torch, t, device="cuda"):
-    """A zeroed workspace for plan tensor t."""
-    return torch.zeros(t.shape, dtype=getattr(torch, TORCH_DTYPES[t.dtype]), device=device)
+def new_workspace(torch, t, device="cuda", align=0):
+    """A zeroed workspace for plan tensor t (at an `align`-byte aligned address when align > 0)."""
+    dt = getattr(torch, TORCH_DTYPES[t.dtype])
+    if not align:
+        return torch.zeros(t.shape, dtype=dt, device=device)
+    return aligned_copy(torch, torch.zeros(t.shape, dtype=dt, device=device), align)
 
 
-def allocate_workspaces(torch, plan, device="cuda"):
-    return {t.name: new_workspace(torch, t, device) for t in plan.tensors.values() if t.kind != "input"}
+def aligned_copy(torch, t, align):
+    """A copy of t whose storage starts at a multiple of `align` bytes (a power of two): the
+    reference's --align-alloc re-basing of weights, capture and workspaces (harness/run_fleet.py)."""
+    if not align:
+        return t
+    assert align & (align - 1) == 0, f"align {align} is not a power of two"
+    nbytes = t.numel() * t.element_size()
+    raw = torch.empty(nbytes + align, dtype=torch.uint8, device=t.device)
+    off = (-raw.data_ptr()) % align
+    out = raw[off:off + nbytes].view(t.dtype).view(t.shape)
+    out.copy_(t)
+    assert out.data_ptr() % align == 0
+    return out
 
 
-def make_tensors(plan, packed, capture, meta, torch, workspaces=None, device="cuda"):
+def allocate_workspaces(torch, plan, align=0, device="cuda"):
+    """Every workspace of the plan, zeroed (the reference's --workspaces-first allocation)."""
+    return {t.name: new_workspace(torch, t, device, align) for t in plan.tensors.values() if t.kind != "input"}
+
+
+def make_tensors(plan, packed, capture, meta, torch, workspaces=None, device="cuda", align=0):
     """name -> torch tensor for every plan tensor: inputs attached (shape-checked), the rest zeroed."""
     host = {}
     workspaces = workspaces or {}
@@ -159,7 +192,7 @@ def make_tensors(plan, packed, capture, meta, torch, workspaces=None, device="cu
         else:
             buf = workspaces.get(t.name)
             if buf is None:
-                buf = new_workspace(torch, t, device)
+                buf = new_workspace(torch, t, device, align)
             assert tuple(buf.shape) == t.shape, (t.name, tuple(buf.shape), t.shape)
             host[t.name] = buf
     return host
@@ -200,12 +233,21 @@ def make_meta(torch, s_max, prompt_ids, n_prompt, device="cuda"):
 
 def plan_json(plan):
     return {"layers": plan.layers, "head": plan.head, "debug": plan.debug, "s_max": plan.s_max,
+            "debug_scores": "scores" in plan.tensors, "attend_tc": plan.attend_tc, "variants": plan.variants,
             "split": plan.split, "head_group": plan.head_group, "dims": plan.dims.to_dict(),
             "tensors": {n: {"shape": list(t.shape), "dtype": t.dtype, "kind": t.kind, "source": t.source}
                         for n, t in plan.tensors.items()},
             "calls": [{"method": c.method, "label": c.label, "status": c.status, "tasks": c.tasks,
-                       "args": {k: (list(v) if isinstance(v, tuple) else v) for k, v in c.args.items()}}
+                       "args": {k: _json_arg(v) for k, v in c.args.items()}}
                       for c in plan.calls]}
+
+
+def _json_arg(v):
+    """A plan argument as JSON: tuples as lists, a row range of a tensor (graph_plan.Rows) as
+    {"tensor": name, "row": first row}."""
+    if isinstance(v, G.Rows):
+        return {"tensor": v.name, "row": v.start}
+    return list(v) if isinstance(v, tuple) else v
 
 
 class MPK:
@@ -251,18 +293,46 @@ class MPK:
         return self.kernel.status(raise_on_error)
 
 
-def build(packed, capture, meta, dims=REAL_DIMS, s_max=1056, layers=27, head=True, debug=False, stop_after=None,
-          split=G.SPLIT, head_group=G.HEAD_GROUP, num_ctas=0, device=None, trace=False, wait_timeout_s=2.0,
-          plan=None, workspaces=None, logit_bias=False, ep=None):
+def build(packed, capture, meta, dims=REAL_DIMS, s_max=1056, layers=27, head=True, debug=False,
+          stop_after=None, debug_scores=False, tile_linears=False, attend_tasks=False, num_workers=296,
+          num_schedulers=8, profiler_tensor=None, align=0, workspaces=None, fuse_norm2=False, fuse_silu=False,
+          probe_before=None, fuse_norm1=False, prefetch=False, gemv_linears=False, linear_grid=None,
+          head_grid=None, gemv_w13=False, merge_tasks=False, merge_halves=1, router_tasks=False,
+          merge_oproj=False, argmax_slices=G.ARGMAX_SLICES, plan=None, *, split=G.SPLIT, head_group=G.HEAD_GROUP,
+          num_ctas=0, device=None, trace=False, wait_timeout_s=2.0, logit_bias=False, ep=None, attend_tc=False,
+          tc_parts=1):
     """On the machine: the plan, its tensors, one library operator per call -> (mpk, host, plan).
-    plan: a ready plan (the stream probe) instead of the model's. ep: an fleet.ep.EpGroup (expert
-    parallelism; every rank calls build with the same arguments and its own group)."""
+
+    The positional and keyword arguments are the reference's (fleet/build_graph.py:561-567, as
+    harness/run_fleet.py:543-553 passes them). The variant switches (tile_linears ... argmax_slices)
+    are checked and recorded (graph_plan.mi300_variants). num_workers / num_schedulers size the
+    reference's MI300X runtime (worker and scheduler blocks); this library runs one persistent CTA
+    per SM (num_ctas, 0 = every SM) and schedules on the host, so they are recorded only.
+    profiler_tensor is the reference runtime's event-timing buffer: per-task timing here is
+    trace=True (mk_trace), so a profiler tensor is refused. probe_before inserts one of the
+    reference's MI300X fault probes and is refused. align re-bases every workspace (and, in the
+    reference's driver, the weights and capture through aligned_copy) on that many bytes.
+
+    B200 keywords: split / head_group (attention partition), num_ctas, device, trace,
+    wait_timeout_s (bound of every device-side wait), logit_bias (injected routing, config 3), ep
+    (an fleet.ep.EpGroup: expert parallelism; every rank calls build with the same arguments and
+    its own group), attend_tc (the tensor-core attention) and tc_parts (its latent-column parts per
+    split). plan: a ready plan (the stream probe)."""
     import torch
     from fleet import mk
 
+    if profiler_tensor is not None:
+        raise ValueError("profiler_tensor: the MI300X runtime's event timing; use trace=True (per-task "
+                         "%globaltimer stamps, mk_trace) on this library")
+    if probe_before:
+        raise ValueError(f"probe_before={probe_before!r}: the MI300X fault probes are not part of the B200 graph")
     if plan is None:
-        plan = G.build_plan(dims, s_max, layers, head, debug, split, head_group, logit_bias=logit_bias,
-                            ep=None if ep is None else (ep.rank, ep.world))
+        plan = G.build_plan(dims, s_max, layers, head, debug, debug_scores, tile_linears, attend_tasks, fuse_norm2,
+                            fuse_silu, fuse_norm1, prefetch, gemv_linears, linear_grid, head_grid, gemv_w13,
+                            merge_tasks, merge_halves, router_tasks, merge_oproj, argmax_slices, split=split,
+                            head_group=head_group, logit_bias=logit_bias,
+                            ep=None if ep is None else (ep.rank, ep.world), attend_tc=attend_tc, tc_parts=tc_parts)
+    plan.variants = dict(plan.variants, num_workers=num_workers, num_schedulers=num_schedulers, align=align)
     if ep is not None:
         workspaces = dict(workspaces or {})
         workspaces["ep_peers"] = ep.peers
@@ -270,7 +340,7 @@ def build(packed, capture, meta, dims=REAL_DIMS, s_max=1056, layers=27, head=Tru
         plan.truncate(stop_after)
     assert not plan.chain_violations(), f"the chain is broken: {plan.chain_violations()}"
     dev = device if device is not None else torch.cuda.current_device()
-    host = make_tensors(plan, packed, capture, meta, torch, workspaces, device=f"cuda:{dev}")
+    host = make_tensors(plan, packed, capture, meta, torch, workspaces, device=f"cuda:{dev}", align=align)
     kernel = mk.MegaKernel(device=dev, num_ctas=num_ctas, trace=trace, wait_timeout_s=wait_timeout_s)
     n_cta = num_ctas or torch.cuda.get_device_properties(dev).multi_processor_count
     index = {}
@@ -323,8 +393,9 @@ class FakeTensor:
 
 class FakeMk:
     """Records operators instead of calling the library (the reference's FakeMPK role)."""
-    OP_EMBED, OP_GEMV, OP_MLA_PREP, OP_MLA_ATTEND, OP_MLA_MERGE_UV, OP_ROUTER, OP_GATEUP, OP_W2_COMBINE, OP_STREAM = range(1, 10)
-    F_NORM, F_RESIDUAL, F_ARGMAX, F_EXPERT, F_STATIC_IDS, F_EP = 1, 2, 4, 8, 16, 32
+    OP_EMBED, OP_GEMV, OP_MLA_PREP, OP_MLA_ATTEND, OP_MLA_MERGE_UV, OP_ROUTER, OP_GATEUP, OP_W2_COMBINE, OP_STREAM, \
+        OP_COPY = range(1, 11)
+    F_NORM, F_RESIDUAL, F_ARGMAX, F_EXPERT, F_STATIC_IDS, F_EP, F_TC = 1, 2, 4, 8, 16, 32, 64
 
     def __init__(self):
         from fleet.mk import P
@@ -343,11 +414,23 @@ class FakeMk:
         return rec
 
 
-def dry_run(dims=REAL_DIMS, s_max=1056, layers=27, head=True, debug=False, stop_after=None, split=G.SPLIT,
-            head_group=G.HEAD_GROUP, ep=None):
+def dry_run(dims=REAL_DIMS, s_max=1056, layers=27, head=True, debug=False, stop_after=None,
+            debug_scores=False, tile_linears=False, attend_tasks=False, fuse_norm2=False, fuse_silu=False,
+            probe_before=None, fuse_norm1=False, prefetch=False, gemv_linears=False, linear_grid=None,
+            head_grid=None, gemv_w13=False, merge_tasks=False, merge_halves=1, router_tasks=False,
+            merge_oproj=False, argmax_slices=G.ARGMAX_SLICES, plan=None, *, split=G.SPLIT,
+            head_group=G.HEAD_GROUP, ep=None, attend_tc=False):
     """The plan and every operator's parameters, without a GPU: returns (plan, recorded ops).
-    ep (rank, world): the expert-parallel plan of that rank."""
-    plan = G.build_plan(dims, s_max, layers, head, debug, split, head_group, ep=ep)
+    Positional arguments as the reference's dry_run (fleet/build_graph.py:786-790, called
+    positionally by harness/run_fleet.py:510-513); ep (rank, world): that rank's
+    expert-parallel plan."""
+    if probe_before:
+        raise ValueError(f"probe_before={probe_before!r}: the MI300X fault probes are not part of the B200 graph")
+    if plan is None:
+        plan = G.build_plan(dims, s_max, layers, head, debug, debug_scores, tile_linears, attend_tasks, fuse_norm2,
+                            fuse_silu, fuse_norm1, prefetch, gemv_linears, linear_grid, head_grid, gemv_w13,
+                            merge_tasks, merge_halves, router_tasks, merge_oproj, argmax_slices, split=split,
+                            head_group=head_group, ep=ep, attend_tc=attend_tc)
     if stop_after:
         plan.truncate(stop_after)
     assert not plan.chain_violations(), plan.chain_violations()

@@ -103,12 +103,13 @@ OUTPUT_ARGS = {
     "embed_layer": ["output"],
     "linear_gemv_layer": ["output", "h_out", "tokens_out"],
     "mla_prep_layer": ["c_kv", "k_pe", "ql_nope", "q_pe"],
-    "mla_attend_layer": ["partials"],
+    "mla_attend_layer": ["partials", "scores"],
     "mla_merge_uv_layer": ["output"],
     "moe_router_layer": ["h", "topk_w", "routing", "mask", "logits", "route_log"],
     "gateup_layer": ["act", "mid", "h_out"],
     "moe_w2_combine_layer": ["output", "out8"],
     "stream_layer": ["dummy"],
+    "copy_layer": ["output"],
 }
 
 
@@ -132,6 +133,8 @@ class Plan:
     debug: bool = False
     split: int = SPLIT
     head_group: int = HEAD_GROUP
+    attend_tc: bool = False
+    variants: dict = field(default_factory=dict)
     tensors: dict = field(default_factory=dict)
     calls: list = field(default_factory=list)
 
@@ -200,24 +203,73 @@ def auto_head_group(n_heads: int, n_splits: int, ctas: int = PLAN_CTAS, d_c: int
     return g
 
 
+ARGMAX_SLICES = 50     # the reference's argmax_partial slice count (its D13); here the argmax is fused
+
+
+def mi300_variants(tile_linears=False, attend_tasks=False, fuse_norm2=False, fuse_silu=False, fuse_norm1=False,
+                   prefetch=False, gemv_linears=False, linear_grid=None, head_grid=None, gemv_w13=False,
+                   merge_tasks=False, merge_halves=1, router_tasks=False, merge_oproj=False,
+                   argmax_slices=ARGMAX_SLICES):
+    """The reference's graph-variant switches (fleet/graph_plan.py:261-267, harness/run_fleet.py
+    --tile-linears ... --merge-oproj), checked and recorded. Each selects one of its MI300X kernel
+    forms or task grids; the B200 graph has one form of each operator, with what the switches turn
+    on always done (the norms, the SwiGLU and the argmax fused into their GEMVs, every linear a
+    GEMV, the experts' gate/up a GEMV, the router a last-arriver task, the merge in head tasks) and
+    the grids chosen by the library. So the values change no operator; they are kept in the plan
+    (plan.variants, plan_json) for the run records."""
+    for name, v in (("linear_grid", linear_grid), ("head_grid", head_grid)):
+        if v is not None and (not isinstance(v, int) or v < 1):
+            raise ValueError(f"{name}: a positive task count or None, not {v!r}")
+    if merge_halves not in (1, 2):
+        raise ValueError(f"merge_halves: 1 or 2, not {merge_halves!r}")
+    if merge_halves != 1 and not merge_tasks:
+        raise ValueError("merge_halves > 1 needs merge_tasks (the reference's rule)")
+    if not isinstance(argmax_slices, int) or argmax_slices < 1:
+        raise ValueError(f"argmax_slices: a positive count, not {argmax_slices!r}")
+    return dict(tile_linears=bool(tile_linears), attend_tasks=bool(attend_tasks), fuse_norm2=bool(fuse_norm2),
+                fuse_silu=bool(fuse_silu), fuse_norm1=bool(fuse_norm1), prefetch=bool(prefetch),
+                gemv_linears=bool(gemv_linears), linear_grid=linear_grid, head_grid=head_grid,
+                gemv_w13=bool(gemv_w13), merge_tasks=bool(merge_tasks), merge_halves=merge_halves,
+                router_tasks=bool(router_tasks), merge_oproj=bool(merge_oproj), argmax_slices=argmax_slices)
+
+
 def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head: bool = True,
-               debug: bool = False, split: int = SPLIT, head_group: int = HEAD_GROUP,
+               debug: bool = False, debug_scores: bool = False, tile_linears: bool = False,
+               attend_tasks: bool = False, fuse_norm2: bool = False, fuse_silu: bool = False,
+               fuse_norm1: bool = False, prefetch: bool = False, gemv_linears: bool = False,
+               linear_grid: int = None, head_grid: int = None, gemv_w13: bool = False, merge_tasks: bool = False,
+               merge_halves: int = 1, router_tasks: bool = False, merge_oproj: bool = False,
+               argmax_slices: int = ARGMAX_SLICES, *, split: int = SPLIT, head_group: int = HEAD_GROUP,
                route_log_rows: int = ROUTE_LOG_ROWS, logit_bias: bool = False, softmax_scale: float = None,
-               ep: tuple = None) -> Plan:
-    """The operator chain for `layers` layers (+ the head). logit_bias: every router adds an
-    injected FP32 bias [E] to its logits (the skewed/uniform routing of config 3). softmax_scale:
-    default q_head_dim^-0.5 times the YaRN mscale^2 of the dims (0.1147213867929261 at REAL_DIMS).
+               ep: tuple = None, attend_tc: bool = False, tc_parts: int = 1) -> Plan:
+    """The operator chain for `layers` layers (+ the head), with the reference's positional
+    arguments (fleet/graph_plan.py:261-267; the variant switches from tile_linears on are
+    checked and recorded, see mi300_variants). debug: a per-layer residual snapshot
+    dbg_x_res_{l} after every layer, read by the next layer (the reference's debug graph).
+    debug_scores: the attention also writes its scaled scores [NH, s_max] (boundary B5).
+    logit_bias: every router adds an injected FP32 bias [E] to its logits (the skewed/uniform
+    routing of config 3). softmax_scale: default q_head_dim^-0.5 times the YaRN mscale^2 of the
+    dims (0.1147213867929261 at REAL_DIMS).
     ep (rank, world): expert parallelism by slot (fleet/ep.py): this rank's gate/up operators and
     down projection cover the slots s (routed, then shared) with s mod world = rank; each
-    down-projection task exchanges its rows with the same task of every peer before it combines."""
+    down-projection task exchanges its rows with the same task of every peer before it combines.
+    attend_tc: the MLA attention on the tensor cores (one task per split for all heads, FP32
+    accumulation in the tensor cores' order: within rounding of the specified-order form);
+    tc_parts: its latent-column parts per split (one task each)."""
+    variants = mi300_variants(tile_linears, attend_tasks, fuse_norm2, fuse_silu, fuse_norm1, prefetch, gemv_linears,
+                              linear_grid, head_grid, gemv_w13, merge_tasks, merge_halves, router_tasks,
+                              merge_oproj, argmax_slices)
     from fleet.capture import softmax_scale as yarn_softmax_scale
     d = dims
     scale = yarn_softmax_scale(d.D_N, d.D_R) if softmax_scale is None else softmax_scale
     assert 1 <= layers <= d.L
-    if head_group is None:
+    if attend_tc:
+        head_group = d.NH
+    elif head_group is None:
         head_group = auto_head_group(d.NH, -(-s_max // split), d_c=d.D_C, d_r=d.D_R)
     assert d.NH % head_group == 0
-    p = Plan(d, s_max, layers, head, debug, split, head_group)
+    p = Plan(d, s_max, layers, head, debug, split, head_group, attend_tc)
+    p.variants = variants
     n_splits = p.n_splits
     # ---- meta, capture and shared activations
     p.t("tokens", (1, s_max), "i64", "input", "meta:tokens")
@@ -230,6 +282,11 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
     p.t("ql_nope", (d.NH, d.D_C))
     p.t("q_pe", (d.NH, d.D_R))
     p.t("partials", (n_splits, d.NH, partials_row(d.D_C)), "f32")
+    if debug_scores:
+        p.t("scores", (d.NH, s_max), "f32")
+    if debug:
+        for l in range(layers):
+            p.t(f"dbg_x_res_{l}", (1, d.H))
     p.t("attn", (1, d.NH * d.D_V))
     if layers >= 1:
         p.t("mid0", (1, 2 * d.I_DENSE))
@@ -257,13 +314,17 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
         p.t(f"W_o_{l}", (d.H, d.NH * d.D_V), kind="input", source=f"W_o_{l}")
         p.t(f"c_kv_{l}", (s_max, d.D_C), kind="input", source=f"capture:c_kv_{l}")
         p.t(f"k_pe_{l}", (s_max, d.D_R), kind="input", source=f"capture:k_pe_{l}")
-        p.op("linear_gemv_layer", f"L{l}.qkva", input="x_res", w_norm=f"w_norm1_{l}", weight=f"W_qkva_{l}",
+        # under debug, the layer reads the previous layer's snapshot (the same values), so the chain
+        # runs through it (the reference's debug graph, fleet/graph_plan.py:433-435)
+        x_in = f"dbg_x_res_{l - 1}" if debug and l > 0 else "x_res"
+        p.op("linear_gemv_layer", f"L{l}.qkva", input=x_in, w_norm=f"w_norm1_{l}", weight=f"W_qkva_{l}",
              output="qkva", h_out="h", norm=True, eps=RMS_EPS)
         p.op("mla_prep_layer", f"L{l}.mla_prep", qkva="qkva", w_kv_norm=f"w_kv_norm_{l}", w_ukT=f"W_ukT_{l}",
              cos="cos", sin="sin", c_kv=f"c_kv_{l}", k_pe=f"k_pe_{l}", ql_nope="ql_nope", q_pe="q_pe", eps=RMS_EPS)
         p.op("mla_attend_layer", f"L{l}.mla_attend", ql_nope="ql_nope", q_pe="q_pe", c_kv=f"c_kv_{l}",
              k_pe=f"k_pe_{l}", partials="partials", softmax_scale=scale, split=split, n_splits=n_splits,
-             head_group=head_group)
+             head_group=head_group, tc=attend_tc, col_parts=tc_parts if attend_tc else 1,
+             **(dict(scores="scores") if debug_scores else {}))
         p.op("mla_merge_uv_layer", f"L{l}.mla_merge_uv", partials="partials", w_uv=f"W_uv_{l}", output="attn",
              split=split, n_splits=n_splits)
         p.op("linear_gemv_layer", f"L{l}.o_proj", input="attn", weight=f"W_o_{l}", residual="x_res",
@@ -306,11 +367,15 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
                 p.op("moe_w2_combine_layer", f"L{l}.w2_combine", deps=(f"L{l}.w13r", f"L{l}.w13s"), input="act8",
                      weight=f"W2_{l}", mask="mask", topk_w="topk_w", residual="x_res", output="x_res",
                      ep=tuple(ep), peers="ep_peers", topk=d.TOPK, layer=l - 1)
+        if debug:
+            p.op("copy_layer", f"L{l}.snapshot", note="debug only: per-layer residual snapshot", input="x_res",
+                 output=f"dbg_x_res_{l}")
     if head:
         p.t("w_final_norm", (d.H,), kind="input", source="w_final_norm")
         p.t("W_lm", (d.V, d.H), kind="input", source="W_lm")
         p.t("logits", (1, d.V))
-        p.op("linear_gemv_layer", "head.lm_head", input="x_res", w_norm="w_final_norm", weight="W_lm",
+        p.op("linear_gemv_layer", "head.lm_head", input=f"dbg_x_res_{layers - 1}" if debug else "x_res",
+             w_norm="w_final_norm", weight="W_lm",
              output="logits", h_out="h", tokens_out="tokens", norm=True, argmax=True, eps=RMS_EPS)
     return p
 

@@ -63,7 +63,9 @@ enum MkOpType {
                              layer 0's gang_linear_silu) */
   MK_OP_W2_COMBINE = 8,   /* out8 = W2 act per slot, x += sum w out8     (gang_moe_w2_silu_mi300.cuh
                              + moe_mul_sum_add) */
-  MK_OP_STREAM = 9        /* read-only bandwidth probe of the weight ring (stream_mi300.cuh:99) */
+  MK_OP_STREAM = 9,       /* read-only bandwidth probe of the weight ring (stream_mi300.cuh:99) */
+  MK_OP_COPY = 10         /* dst = src, n BF16 values (the debug per-layer residual snapshot, the
+                             reference's copy_layer in fleet/graph_plan.py:565-567) */
 };
 
 /* MkOp.flags */
@@ -112,8 +114,12 @@ enum { /* MK_OP_MLA_PREP */ MK_P_PREP_QKVA = 0, MK_P_PREP_WKVNORM = 1, MK_P_PREP
        MK_I_PREP_NH = 0, MK_I_PREP_DN = 1, MK_I_PREP_DR = 2, MK_I_PREP_DC = 3, MK_I_PREP_SMAX = 4 };
 enum { /* MK_OP_MLA_ATTEND */ MK_P_ATT_QLNOPE = 0, MK_P_ATT_QPE = 1, MK_P_ATT_CKV = 2, MK_P_ATT_KPE = 3,
        MK_P_ATT_PARTIALS = 4,
+       MK_P_ATT_SCORES = 5, /* optional [nh, s_max] FP32: the scaled scores of every live row (the
+                               reference's debug_scores boundary B5, fleet/build_graph.py:75-81) */
        MK_I_ATT_NH = 0, MK_I_ATT_DC = 1, MK_I_ATT_DR = 2, MK_I_ATT_SMAX = 3, MK_I_ATT_SPLIT = 4,
-       MK_I_ATT_HGROUP = 5, MK_I_ATT_NSPLITS = 6, MK_I_ATT_PROW = 7 };
+       MK_I_ATT_HGROUP = 5, MK_I_ATT_NSPLITS = 6, MK_I_ATT_PROW = 7,
+       MK_I_ATT_CPARTS = 8 /* MK_F_TC: latent-column parts per split (1, 2, 4 or 8): task (q, j) computes
+                              the split's scores and softmax and the P.V columns of part q */ };
 enum { /* MK_OP_MLA_MERGE_UV */ MK_P_MRG_PARTIALS = 0, MK_P_MRG_WUV = 1, MK_P_MRG_OUT = 2,
        MK_I_MRG_NH = 0, MK_I_MRG_DV = 1, MK_I_MRG_DC = 2, MK_I_MRG_SPLIT = 3, MK_I_MRG_NSPLITS = 4,
        MK_I_MRG_PROW = 5 };
@@ -147,6 +153,7 @@ typedef struct MkEpPeers {
   int32_t reserved[3];
 } MkEpPeers;
 enum { /* MK_OP_STREAM */ MK_P_ST_W = 0, MK_P_ST_OUT = 1, MK_I_ST_ROWS = 0, MK_I_ST_K = 1 };
+enum { /* MK_OP_COPY */ MK_P_CP_SRC = 0, MK_P_CP_DST = 1, MK_I_CP_N = 0 };
 
 typedef struct MkConfig {
   int32_t device;            /* CUDA device ordinal */

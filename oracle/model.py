@@ -105,15 +105,18 @@ class OracleModel:
                 rec.update({"head.norm": h, "head.logits": logits, "head.token": tok})
         return tok, x, rec
 
-    def generate(self, tokens, pos0, iters, cache, cos, sin, record_last=False):
+    def generate(self, tokens, pos0, iters, cache, cos, sin, record_last=False, on_step=None):
         """Greedy decode: iteration i reads tokens[pos0 + i] and writes tokens[pos0 + i + 1].
-        Returns (ids, route_log [iters][moe layers] of the TOPK ids, last record)."""
+        Returns (ids, route_log [iters][moe layers] of the TOPK ids, last record). on_step(i, rec)
+        sees every iteration's record (router probabilities, logits) as it is made."""
         ids, routes, rec = [], [], None
         for i in range(iters):
             pos = pos0 + i
             last = record_last and i == iters - 1
             tok, _, r = self.step(int(tokens[pos]), pos, cache, cos, sin, record=True)
             routes.append([r[f"L{l}.mask"][:self.d.TOPK].tolist() for l in range(1, self.layers)])
+            if on_step is not None:
+                on_step(i, r)
             if last:
                 rec = r
             tokens[pos + 1] = tok

@@ -23,6 +23,7 @@ import pytest
 import torch
 
 from gpu_helpers import DeviceWeightBits, u16
+from oracle import numpy_ref as R
 from oracle.detmath import bf16_bits
 from oracle.model import OracleModel
 
@@ -32,8 +33,10 @@ ITERS = 32
 GOLDEN = Path(__file__).resolve().parent / "golden" / "c1_greedy_ids.json"
 
 
-def oracle_greedy(w, pos0, iters, cache_bits, cos, sin, tokens):
-    """The oracle's own greedy decode of `iters` tokens from position pos0 (its own cache)."""
+def oracle_greedy(w, pos0, iters, cache_bits, cos, sin, tokens, margins=None):
+    """The oracle's own greedy decode of `iters` tokens from position pos0 (its own cache).
+    margins (a list): per iteration, the logit gap between the best and second token relative to
+    the largest |logit|, and per MoE layer the router probabilities (for the tie rule)."""
     from fleet.capture import softmax_scale
     from fleet.graph_plan import SPLIT
     d = w.dims
@@ -41,47 +44,126 @@ def oracle_greedy(w, pos0, iters, cache_bits, cos, sin, tokens):
     m = OracleModel(d, dw.get, dw.get_expert, softmax_scale=softmax_scale(d.D_N, d.D_R), split=SPLIT)
     cache = {k: (v.astype(np.uint32) << 16).view(np.float32) for k, v in cache_bits.items()}
     tokens = tokens.copy()
-    ids, routes, rec = m.generate(tokens, pos0, iters, cache, cos, sin, record_last=True)
+    def note(i, r):
+        if margins is not None:
+            lg = r["head.logits"].astype(np.float64)
+            top2 = np.sort(lg)[-2:]
+            probs = {l: R.softmax_det(r[f"L{l}.router_logits"]) for l in range(1, d.L)}
+            margins.append(dict(gap=float((top2[1] - top2[0]) / np.abs(lg).max()), probs=probs))
+
+    ids, routes, rec = m.generate(tokens, pos0, iters, cache, cos, sin, record_last=True, on_step=note)
     return ids, routes, rec, cache
 
 
-def test_c1_27_layers_32_greedy_tokens_one_launch_match_oracle():
+@pytest.fixture(scope="module")
+def c1():
+    """Config 1's workload on the device and the oracle's own 32-step greedy decode of it."""
     from fleet import build_graph as B
     from fleet.workload import greedy_decode
     w = greedy_decode(DEV, new_tokens=ITERS)
-    d = w.dims
     cache0 = {k: u16(v) for k, v in w.capture.items() if k.startswith(("c_kv_", "k_pe_"))}
     meta = B.make_meta(torch, w.s_max, w.prompt, w.n_prompt, device=DEV)
-    mpk, host, plan = B.build(w.packed, w.capture, meta, dims=d, s_max=w.s_max, layers=d.L, head=True)
+    t0 = time.time()
+    cos, sin = (w.capture[k].float().cpu().numpy() for k in ("cos", "sin"))
+    tokens = meta["tokens"][0].cpu().numpy().copy()
+    margins = []
+    ids, routes, rec, ocache = oracle_greedy(w, w.first_pos, ITERS, cache0, cos, sin, tokens, margins)
+    if GOLDEN.exists():
+        assert ids == json.loads(GOLDEN.read_text())["ids"], "the oracle's ids moved from the committed list"
+    return dict(w=w, cache0=cache0, ids=ids, routes=routes, rec=rec, ocache=ocache, oracle_s=time.time() - t0,
+                margins=margins)
+
+
+def run_c1(c1, **build_kw):
+    """One launch of all 32 iterations from the workload's initial state."""
+    from fleet import build_graph as B
+    w = c1["w"]
+    d = w.dims
+    for k, v in c1["cache0"].items():            # the initial cache (an earlier run appended rows)
+        w.capture[k].view(torch.int16).copy_(torch.from_numpy(v.view(np.int16)))
+    meta = B.make_meta(torch, w.s_max, w.prompt, w.n_prompt, device=DEV)
+    mpk, host, plan = B.build(w.packed, w.capture, meta, dims=d, s_max=w.s_max, layers=d.L, head=True, **build_kw)
     mpk.compile()
     assert plan.n_ops == 243 and plan.layers == 27
     mpk()                                        # all 32 iterations in one launch
     st = mpk.status()
     assert st["error"] == 0 and st["launches"] == 1 and st["generation"] == ITERS, st
-    pos0 = w.first_pos
-    ids = meta["tokens"][0, w.n_prompt:w.n_prompt + ITERS].tolist()
-    route_log = host["route_log"].cpu().numpy()                 # [32, L - 1, 8], row = iteration
-    gpu_cache = {k: u16(w.capture[k]) for k in cache0}
-    logits = u16(host["logits"][0])
+    out = dict(ids=meta["tokens"][0, w.n_prompt:w.n_prompt + ITERS].tolist(),
+               route_log=host["route_log"].cpu().numpy(),             # [32, L - 1, 8], row = iteration
+               cache={k: u16(w.capture[k]) for k in c1["cache0"]}, logits=u16(host["logits"][0]))
+    mpk.kernel.close()
+    return out
 
-    t0 = time.time()
-    cos, sin = (w.capture[k].float().cpu().numpy() for k in ("cos", "sin"))
-    tokens = meta["tokens"][0].cpu().numpy().copy()
-    tokens[w.n_prompt:] = 0
-    want_ids, want_routes, rec, ocache = oracle_greedy(w, pos0, ITERS, cache0, cos, sin, tokens)
-    t_oracle = time.time() - t0
 
-    assert ids == want_ids, f"greedy ids differ: got {ids}, oracle {want_ids}"
+def check_routes(c1, got):
+    d = c1["w"].dims
     for i in range(ITERS):
         for j in range(d.L - 1):
-            got = route_log[i, j, :d.TOPK].tolist()
-            assert got == want_routes[i][j], f"iteration {i}, MoE layer {j + 1}: routes {got} != {want_routes[i][j]}"
-        assert route_log[i, :, d.TOPK:].tolist() == [list(range(d.E, d.E_TOTAL))] * (d.L - 1)
-    for k, v in gpu_cache.items():
+            r = got["route_log"][i, j, :d.TOPK].tolist()
+            assert r == c1["routes"][i][j], f"iteration {i}, MoE layer {j + 1}: routes {r} != {c1['routes'][i][j]}"
+        assert got["route_log"][i, :, d.TOPK:].tolist() == [list(range(d.E, d.E_TOTAL))] * (d.L - 1)
+
+
+def test_c1_27_layers_32_greedy_tokens_one_launch_match_oracle(c1):
+    got = run_c1(c1)
+    pos0 = c1["w"].first_pos
+    assert got["ids"] == c1["ids"], f"greedy ids differ: got {got['ids']}, oracle {c1['ids']}"
+    check_routes(c1, got)
+    for k, v in got["cache"].items():
         rows = slice(pos0, pos0 + ITERS)
-        bad = np.nonzero(v[rows] != bf16_bits(ocache[k][rows]))
+        bad = np.nonzero(v[rows] != bf16_bits(c1["ocache"][k][rows]))
         assert bad[0].size == 0, f"{k}: {bad[0].size} cache values differ (first rows {bad[0][:4] + pos0})"
-    assert np.array_equal(logits, bf16_bits(rec["head.logits"])), "last token's logits differ"
-    if GOLDEN.exists():
-        assert want_ids == json.loads(GOLDEN.read_text())["ids"], "the oracle's ids moved from the committed list"
-    print(f"c1: 32 greedy ids equal the oracle's ({t_oracle:.0f} s of oracle); ids {ids}")
+    assert np.array_equal(got["logits"], bf16_bits(c1["rec"]["head.logits"])), "last token's logits differ"
+    print(f"c1 exact: 32 greedy ids equal the oracle's ({c1['oracle_s']:.0f} s of oracle); ids {got['ids']}")
+
+
+TIE_REL = 2e-2   # the north-star BF16 tolerance, as a relative band for near-ties
+
+
+def test_c1_tensor_core_attention_agrees_up_to_near_ties(c1):
+    """The same decode with the MLA attention on the tensor cores (FP32 accumulation in the
+    tensor cores' order, so every attention output differs from the specified-order one in the last
+    bits). Judged as the reference's harness/compare.py judges a run against its reference:
+    * ids: equal up to the first divergence, and the divergence (if any) must come at a step whose
+      oracle logits have their two best tokens within TIE_REL of the largest |logit| (a near-tie
+      that a last-bit difference can flip; compare_ids, :161);
+    * routes: before the first id divergence, a mismatch must be one expert swapped for one whose
+      oracle router probability is within TIE_REL of the larger (a tie), or come after such a tie
+      (a cascade), as compare_route_log classifies them (:181-236);
+    * every cache row appended before the divergence within 2e-2 of the oracle's (rel_err, the L2
+      norm of the difference over the oracle row's: the reference's boundary metric).
+    The exact form (the default) is the one whose 32 ids equal the oracle's; this form is the
+    tensor-core alternative and states how far it agrees."""
+    from oracle.detmath import from_bf16_bits
+    got = run_c1(c1, attend_tc=True)
+    pos0, d = c1["w"].first_pos, c1["w"].dims
+    first = next((i for i in range(ITERS) if got["ids"][i] != c1["ids"][i]), ITERS)
+    if first < ITERS:
+        gap = c1["margins"][first]["gap"]
+        assert gap <= TIE_REL, f"ids diverge at step {first} where the oracle's top-2 gap is {gap:.3g} (not a tie)"
+    ties = cascades = 0
+    for i in range(min(first + 1, ITERS)):
+        for j in range(d.L - 1):
+            r = sorted(c1["routes"][i][j])
+            f = sorted(got["route_log"][i, j, :d.TOPK].tolist())
+            if r == f:
+                continue
+            left, came = sorted(set(r) - set(f)), sorted(set(f) - set(r))
+            p = c1["margins"][i]["probs"][j + 1]
+            if len(left) == 1 and abs(float(p[left[0]]) - float(p[came[0]])) <= TIE_REL * max(p[left[0]], p[came[0]]):
+                ties += 1
+            else:
+                assert ties or cascades, f"step {i}, MoE layer {j + 1}: routes {f} vs {r} is no tie"
+                cascades += 1
+    worst = 0.0
+    for k, v in got["cache"].items():
+        n = min(first, ITERS)
+        g = from_bf16_bits(v[pos0:pos0 + n]).astype(np.float64)
+        o = c1["ocache"][k][pos0:pos0 + n].astype(np.float64)
+        rel = np.linalg.norm(g - o, axis=1) / np.maximum(np.linalg.norm(o, axis=1), 1e-30)
+        if rel.size:
+            worst = max(worst, float(rel.max()))
+            assert rel.max() <= 2e-2, f"{k}: cache rows differ by rel_err {rel.max():.3g}"
+    print(f"c1 tensor cores: ids equal for {first} of {ITERS} steps"
+          + (f" (the oracle's top-2 gap at step {first}: {c1['margins'][first]['gap']:.3g})" if first < ITERS else "")
+          + f"; route ties {ties}, cascades {cascades}; worst cache row {worst:.3g}")

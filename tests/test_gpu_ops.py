@@ -216,6 +216,56 @@ def test_mla_attend_merge_long_context(mk, B, ctx, split, hg):
     assert_bits_equal(attn, R.mla_merge_uv(want, np32(W_uv), pos, split=split), "attn")
 
 
+# The tensor-core form (MK_F_TC): all 16 heads of a split in one task, mma.sync with FP32
+# accumulation in the tensor cores' order. Config 2's sweep: contexts 1K..32K, 8/16/32 splits (a
+# split of ctx / n rows, processed in chunks of 96 rows with an online softmax), plus positions
+# whose own row is alone in its chunk or split. Within the north-star tolerance of the oracle's
+# specified-order result: partials and attn max-abs error <= 2e-2 of the largest value, lse
+# within 1e-3, cosine >= 0.9999.
+def _close(got, want, what, rel=2e-2, cos=0.9999):
+    got = np.asarray(got, np.float64).reshape(-1)
+    want = np.asarray(want, np.float64).reshape(-1)
+    err = np.abs(got - want).max()
+    scale = np.abs(want).max()
+    c = float(got @ want / (np.linalg.norm(got) * np.linalg.norm(want) + 1e-30))
+    assert err <= rel * scale and c >= cos, f"{what}: max err {err:.3g} (scale {scale:.3g}), cosine {c:.6f}"
+
+
+@pytest.mark.parametrize("ctx,n_splits,pos,parts", [
+    (1024, 8, None, 1), (1024, 16, None, 1), (1024, 32, None, 1), (4096, 8, None, 1), (4096, 16, None, 1),
+    (4096, 32, None, 1), (16384, 8, None, 1), (16384, 32, None, 1), (32768, 8, None, 1), (32768, 16, None, 1),
+    (32768, 32, None, 1), (1056, 11, 1055 - 96, 1), (1056, 11, 96 * 3, 1), (1056, 11, 0, 1), (1056, 11, 5, 1),
+    (1056, 11, 1024, 1), (1024, 16, None, 2), (1024, 16, None, 4), (4096, 16, None, 8), (1056, 11, 5, 4),
+    (1056, 33, 1024, 4)])
+def test_mla_attend_tc_matches_oracle(mk, B, ctx, n_splits, pos, parts):
+    nh, d_r, d_c, d_v = 16, 64, 512, 128
+    s_max = ctx
+    split = -(-ctx // n_splits)
+    pos = ctx - 1 if pos is None else pos
+    g = gen(3)
+    ql = rnd_bf16(g, nh, d_c)
+    qp = rnd_bf16(g, nh, d_r)
+    c_kv = rnd_bf16(g, s_max, d_c)
+    k_pe = rnd_bf16(g, s_max, d_r)
+    W_uv = rnd_bf16(g, nh, d_v, d_c, std=0.05)
+    from fleet.capture import softmax_scale
+    from fleet.graph_plan import partials_row
+    partials = torch.zeros((n_splits, nh, partials_row(d_c)), dtype=torch.float32, device=DEV)
+    attn = torch.zeros(nh * d_v, dtype=torch.bfloat16, device=DEV)
+    scale = softmax_scale(128, d_r)
+    ops = [B.mla_attend_layer(mk, None, ql, qp, c_kv, k_pe, partials, scale, split, n_splits, nh, tc=True,
+                              col_parts=parts),
+           B.mla_merge_uv_layer(mk, None, partials, W_uv, attn, split, n_splits)]
+    run_ops(mk, ops, step=pos - 1)
+    want = R.mla_attend(np32(ql), np32(qp), np32(c_kv), np32(k_pe), pos, scale, split=split, n_splits=n_splits)
+    got = partials.cpu().numpy()
+    live = -(-(pos + 1) // split)
+    assert np.all(np.isneginf(got[live:, :, d_c])) and not np.any(got[live:, :, :d_c]), "dead splits"
+    _close(got[:live, :, :d_c], want[:live, :, :d_c], "partials o")
+    assert np.abs(got[:live, :, d_c] - want[:live, :, d_c]).max() <= 1e-3, "partials lse"
+    _close(np32(attn), R.mla_merge_uv(want, np32(W_uv), pos, split=split), "attn")
+
+
 def _router_inputs(g, E=64, H=2048):
     x = rnd_bf16(g, H)
     w_norm = (1.0 + 0.5 * torch.randn(H, generator=g, device=DEV)).to(torch.bfloat16)
