@@ -3,6 +3,7 @@ model's own modules (fixtures), and the packed-weight layout and byte accounting
 import json
 
 import numpy as np
+import pytest
 import torch
 
 from fleet import capture as C
@@ -111,6 +112,26 @@ def test_checkpoint_loader_matches_state_dict(golden, tmp_path):
     assert got.keys() == want.keys()
     for k in want:
         assert got[k].dtype == torch.bfloat16 and torch.equal(got[k], want[k]), k
+
+
+def test_checkpoint_reader_single_file_and_dtype(golden, tmp_path):
+    """The reader without an index (one model.safetensors), and its refusal of non-BF16 weights."""
+    from safetensors.torch import save_file
+    fx = golden("hf_tiny.npz")
+    cfg = json.loads(str(fx["config"]))
+    d = P.Dims.from_config(cfg)
+    sd = {k[2:]: torch.from_numpy(fx[k].astype(np.int16)).view(torch.bfloat16) for k in fx.files if k.startswith("w:")}
+    save_file({k: v.contiguous() for k, v in sd.items()}, str(tmp_path / "model.safetensors"))
+    (tmp_path / "config.json").write_text(json.dumps(cfg))
+    got, want = P.pack_all(tmp_path), P.pack_state_dict(d, sd)
+    assert got.keys() == want.keys() and all(torch.equal(got[k], want[k]) for k in want)
+    rd = P.SafetensorsDir(tmp_path)
+    assert rd.names() == sorted(sd)
+    bad = tmp_path / "f32"
+    bad.mkdir()
+    save_file({"x": torch.zeros(4)}, str(bad / "model.safetensors"))
+    with pytest.raises(ValueError):
+        P.SafetensorsDir(bad).tensor("x")
 
 
 def test_router_biases_zipf_and_uniform():
