@@ -15,8 +15,9 @@ D2H every step), the roofline of the kernel against the measured HBM copy bandwi
 (MEASURED_PEAKS.json), the CPU oracle's time for the same work on this host, the clocks seen.
 
 `--impl reference` times the reference's CPU path (the oracle port of harness/numpy_ref.py
-composed into the decode step; the reference's own runtime is HIP for MI300X and its Fleet
-submodule is absent, so nothing else of it can run here).
+composed into the decode step, its row dots and attention in C on every host core; the
+reference's own runtime is HIP for MI300X and its Fleet submodule is absent, so nothing else of it
+can run here): W untimed and K timed whole decode tokens.
 """
 import argparse
 import json
@@ -45,10 +46,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c1", choices=["c1", "c0", "c2"],
+                    help="c1: the decode step (the metric); c0: one MoE layer at position 1024; c2: the MLA "
+                         "attention sweep (contexts 1K..32K, 8/16/32 splits); c0 and c2 print one line per case")
     ap.add_argument("--layers", type=int, default=27)
     ap.add_argument("--ctx", type=int, default=N_PROMPT,
                     help="prompt length (latent-cache rows + 1); 8192 is config 4's context (cache seed 5)")
-    ap.add_argument("--cpu-sample-s", type=float, default=20.0, help="bound of the CPU baseline sample")
+    ap.add_argument("--cpu-sample-s", type=float, default=12.0, help="bound of the CPU baseline sample (s)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--routing", default="natural", choices=["natural", "uniform", "zipf"],
                     help="config 3's injected router logits (seed 4): uniform, or Zipf s=1.2 over the experts")
@@ -56,6 +60,7 @@ def parse():
                     help="MLA attention form: the bit-exact FP32 CUDA-core tasks, or the tensor-core tasks")
     ap.add_argument("--split", type=int, default=None, help="cache rows per attention split (default: the plan's)")
     ap.add_argument("--tc-parts", type=int, default=1, help="tensor-core attention: latent-column parts per split")
+    ap.add_argument("--op-tasks", default="", help="task counts per operator kind, e.g. router=16,qkva=96")
     ap.add_argument("--trace", action="store_true",
                     help="record per-task %%globaltimer stamps and print a per-operator breakdown of the last "
                          "token to stderr (the timed numbers then include the stamping)")
@@ -203,10 +208,18 @@ def build_model(args, device, layers, ep=None):
     extra = {} if args.split is None else dict(split=args.split)
     mpk, host, plan = B.build(packed, capture, meta, dims=d, s_max=s_max, layers=layers, head=True,
                               trace=args.trace, ep=ep, logit_bias=routing != "natural",
-                              attend_tc=args.attend == "tc", tc_parts=args.tc_parts, **extra)
+                              attend_tc=args.attend == "tc", tc_parts=args.tc_parts, op_tasks=op_tasks(args), **extra)
     mpk.compile()
     torch.cuda.synchronize()
+    build_model.workload = w
     return d, packed, capture, meta, mpk, host, plan, time.time() - t0
+
+
+def op_tasks(args):
+    """--op-tasks kind=n,... as a dict (None when empty)."""
+    if not args.op_tasks:
+        return None
+    return {k: int(v) for k, v in (kv.split("=") for kv in args.op_tasks.split(","))}
 
 
 def ids_check(meta, args):
@@ -312,75 +325,63 @@ def time_e2e(mpk, meta, steps, torch, stream):
     return e0.elapsed_time(e1) / steps, wall
 
 
-def cpu_baseline(packed, capture, meta, d, plan, budget_s, n_prompt=N_PROMPT):
-    """The oracle (the reference's NumPy path, restated) on this host's cores for a bounded
-    sample of one decode token: embedding, layer 0 (dense), MoE layers 1..m and the head, timed
-    per part and extrapolated to the 26 MoE layers of a token."""
-    import numpy as np
-    import torch
+class CpuDecoder:
+    """The CPU oracle decoding the same workload on this host: harness/numpy_ref.py's arithmetic
+    (oracle/numpy_ref.py) composed into the decode step (oracle/model.py), its row dots and
+    attention in C over the BF16 weights (oracle/detdot.c, one thread per host core unless
+    ORACLE_THREADS says otherwise). The weights are copied to host memory once (31.4 GB at
+    REAL_DIMS), outside any timing; each token is timed whole (embedding, every layer, head)."""
 
-    from fleet.capture import softmax_scale
-    from oracle.model import OracleModel
+    def __init__(self, w, split):
+        import numpy as np
+        import torch
+        from fleet.capture import softmax_scale
+        from oracle import detmath
+        from oracle.model import OracleModel
 
-    np32 = lambda t: t.detach().float().cpu().numpy()  # noqa: E731
-    cache = {}
-    gets = {}
+        def u16(t):
+            return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
 
-    def get(name):
-        if name not in gets:
-            gets[name] = np32(packed[name])
-        return gets[name]
+        t0 = time.time()
+        self.host = {k: u16(v) for k, v in w.packed.items()}
+        d = w.dims
+        self.model = OracleModel(d, self.host.__getitem__, lambda n, e: self.host[n][e],
+                                 softmax_scale=softmax_scale(d.D_N, d.D_R), split=split)
+        self.cache = {k: (u16(v).astype(np.uint32) << 16).view(np.float32) for k, v in w.capture.items()
+                      if k.startswith(("c_kv_", "k_pe_"))}
+        self.cos, self.sin = (w.capture[k].float().cpu().numpy() for k in ("cos", "sin"))
+        self.tokens = np.zeros(w.s_max, np.int64)
+        self.tokens[:w.n_prompt] = w.prompt
+        self.pos = w.first_pos
+        self.copy_s = time.time() - t0
+        self.native = detmath._od() is not None
+        self.threads = int(os.environ.get("ORACLE_THREADS", os.cpu_count() or 1)) if self.native else 1
 
-    def get_expert(name, e):
-        key = (name, e)
-        if key not in gets:
-            gets[key] = np32(packed[name][e])
-        return gets[key]
-
-    m_layers = 3
-    m = OracleModel(d, get, get_expert, softmax_scale=softmax_scale(d.D_N, d.D_R), split=plan.split,
-                    layers=m_layers)
-    pos = n_prompt - 1
-    for l in range(m_layers):
-        cache[f"c_kv_{l}"] = np32(capture[f"c_kv_{l}"])
-        cache[f"k_pe_{l}"] = np32(capture[f"k_pe_{l}"])
-    cos, sin = np32(capture["cos"]), np32(capture["sin"])
-    # warm the host copies of every weight the sample touches (not timed)
-    for k in ("W_embed", "W_lm", "w_final_norm"):
-        get(k)
-    for l in range(m_layers):
-        for k in ("w_norm1", "w_norm2", "W_qkva", "w_kv_norm", "W_ukT", "W_uv", "W_o"):
-            get(f"{k}_{l}")
-    get("W_gu_0"), get("W_down_0")
-    for l in range(1, m_layers):
-        get(f"W_gate_{l}")
-        for e in range(d.E_TOTAL):
-            get_expert(f"W13_{l}", e), get_expert(f"W2_{l}", e)
-    from oracle import numpy_ref as R
-    x = R.embed(get("W_embed"), int(meta["tokens"][0, pos]))
-    t = {}
-    t0 = time.perf_counter()
-    x = m.attention(0, x, cache, cos, sin, pos, None)
-    x = m.dense_mlp(x, None)
-    t["layer0"] = time.perf_counter() - t0
-    moe = []
-    for l in range(1, m_layers):
+    def token(self):
+        """Decode one token; returns its wall time (s)."""
         t0 = time.perf_counter()
-        x = m.attention(l, x, cache, cos, sin, pos, None)
-        x = m.moe(l, x, None)
-        moe.append(time.perf_counter() - t0)
-        if sum(moe) + t["layer0"] > budget_s:
-            break
-    t0 = time.perf_counter()
-    R.lm_head_argmax(x, get("w_final_norm"), get("W_lm"))
-    t["head"] = time.perf_counter() - t0
-    t_moe = sum(moe) / len(moe)
-    per_token = t["layer0"] + (d.L - 1) * t_moe + t["head"]
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    sample = (f"one decode token at position {pos}: layer 0 (dense) + {len(moe)} MoE layer(s) + head timed "
-              f"({t['layer0'] + sum(moe) + t['head']:.1f} s), MoE layers extrapolated to {d.L - 1}")
-    return {"value": per_token * 1e3, "unit": "ms/token", "cores": threads, "kind": "port", "sample": sample,
-            "parts_s": {"layer0": t["layer0"], "moe_layer": t_moe, "head": t["head"]}}
+        tok, _, _ = self.model.step(int(self.tokens[self.pos]), self.pos, self.cache, self.cos, self.sin)
+        dt = time.perf_counter() - t0
+        self.tokens[self.pos + 1] = tok
+        self.pos += 1
+        return dt
+
+    def describe(self, n):
+        return (f"{n} whole decode tokens of the 27-layer model from position {self.pos - n} (every layer and the "
+                f"head timed, nothing extrapolated); weights held as BF16 in host memory "
+                f"(copied in {self.copy_s:.0f} s, not timed); {'C row dots and attention' if self.native else 'numpy'}"
+                f" on {self.threads} thread(s) of {os.cpu_count()} host cores")
+
+
+def cpu_baseline(w, split, budget_s):
+    """A bounded sample of the same workload on the host cores: whole tokens until budget_s."""
+    dec = CpuDecoder(w, split)
+    times = []
+    while not times or (sum(times) < budget_s and len(times) < 16):
+        times.append(dec.token())
+    v = sum(times) / len(times) * 1e3
+    return {"value": round(v, 1), "unit": "ms/token", "cores": dec.threads, "kind": "port",
+            "sample": dec.describe(len(times))}
 
 
 def roofline(d, ms_per_token, ctx, bw_peak, peak_kind, world=1):
@@ -429,6 +430,7 @@ def run_ours(args):
         # s mod N = r; every rank holds every expert's weights and runs the rest of the graph
         ep = EpGroup(rank, ws, local, D.N_SLOTS, D.H, args.layers - 1, all_gather)
     d, packed, capture, meta, mpk, host, plan, t_setup = build_model(args, device, args.layers, ep)
+    wl = build_model.workload
     stream = torch.cuda.Stream(device=device)
     mpk.step = args.ctx - 2
     for _ in range(args.warmup):
@@ -465,9 +467,9 @@ def run_ours(args):
     ctx = ctx0 + args.steps // 2
     roof = roofline(d, ms, ctx, bw, kind, ws)
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_baseline(packed, capture, meta, d, plan, args.cpu_sample_s, args.ctx)
+            cpu = cpu_baseline(wl, plan.split, args.cpu_sample_s)
         except MemoryError as e:            # the host could not hold the sample's weights
             cpu = {"value": None, "unit": "ms/token", "error": f"MemoryError: {e}"}
     if dist:
@@ -495,6 +497,7 @@ def run_ours(args):
                    "attention": ("tensor cores (mma.sync BF16, FP32 accumulation)" if args.attend == "tc" else
                                  "FP32 CUDA cores, specified summation order (bit-exact)"),
                    "split": plan.split, "tc_parts": args.tc_parts if args.attend == "tc" else None,
+                   "op_tasks": op_tasks(args),
                    "tokens_per_s": round(1e3 / ms, 2)},
         "tokens_per_s": round(1e3 / ms, 2),
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms/token", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
@@ -512,44 +515,158 @@ def run_ours(args):
 
 
 def run_reference(args):
+    """The reference arm: the reference's CPU path for this workload (its NumPy arithmetic, restated
+    by the oracle with the GEMVs and attention in C; the reference's own runtime is HIP for MI300X
+    and cannot run here) on this host's cores, W untimed tokens then K timed ones, each a whole
+    decode token. Rank 0 only."""
     ws, rank, local = dist_env()
     if rank != 0:
         return
     import torch
-    # the oracle port needs the same synthetic weights; they are generated on the GPU (as for our
-    # arm) and copied to host memory for the parts the sample touches
+    from fleet import graph_plan as G
+    from fleet.workload import greedy_decode
     device = "cuda:0" if torch.cuda.is_available() else "cpu"
-    from fleet.pack_weights import REAL_DIMS, synthetic_packed
-    from fleet.capture import make_capture
+    # the weights are the seeded synthetic ones of our arm (drawn by the CUDA generator on the GPU,
+    # then copied to host memory once)
+    w = greedy_decode(device, n_prompt=args.ctx, new_tokens=args.warmup + args.steps + 2, layers=args.layers)
+    dec = CpuDecoder(w, args.split or G.SPLIT)
+    del w
+    torch.cuda.empty_cache()
+    for _ in range(args.warmup):
+        dec.token()
+    times = [dec.token() for _ in range(args.steps)]
+    v = sum(times) / len(times) * 1e3
+    sample = dec.describe(args.steps)
+    out = {"metric": METRIC, "value": round(v, 2), "unit": "ms/token", "n_gpus": ws, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(v, 2), "higher_is_better": False, "impl": "reference",
+           "scaling": "strong", "vs_baseline": None,
+           "dtype": "bf16 weights, FP32 accumulation (the reference's NumPy arithmetic; oracle port)",
+           "data": "synthetic: the same seeded weights, cache and prompt as our arm",
+           "config": {"workload": "C1: 27-layer DeepSeek-V2-Lite-shaped greedy decode, batch 1, on the host CPU",
+                      "layers": args.layers, "ctx": [args.ctx + args.warmup, args.ctx + args.warmup + args.steps - 1]},
+           "cpu_baseline": {"value": round(v, 2), "unit": "ms/token", "cores": dec.threads, "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": round(v, 2), "unit": "ms/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "ms_per_step_minmax": [round(min(times) * 1e3, 1), round(max(times) * 1e3, 1)]}
+    print(json.dumps(out))
+
+
+# ---------------------------------------------------------------------------------------------
+# config 0 and config 2: the operators of one layer, and the attention alone
+
+
+def _flush_l2(torch, buf):
+    buf.add_(1)            # 256 MiB written between timed launches: more than the 126 MB L2
+
+
+def _time_kernel(torch, k, step, steps, warmup, before=None):
+    """Device time (us) of single-iteration launches of handle k at position step + 1, L2 flushed
+    between them; before(): per-launch input reset, outside the timed region."""
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device="cuda")
+    s = torch.cuda.Stream()
+    times = []
+    for i in range(warmup + steps):
+        if before:
+            before()
+        _flush_l2(torch, flush)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        k.launch(1, step, s)
+        e1.record(s)
+        torch.cuda.synchronize()
+        if i >= warmup:
+            times.append(e0.elapsed_time(e1) * 1e3)
+    assert k.status()["error"] == 0
+    return times
+
+
+def run_c2(args):
+    """Config 2: the MLA decode attention (split-KV partials + merge + W_uv) alone, 16 heads of 576
+    against one shared latent head, q and KV ~N(0,1) seed 3, at contexts 1K..32K with 8, 16 and 32
+    splits, in both forms (the exact CUDA-core form where a split fits its ring, <= 168 rows)."""
+    import torch
+    from fleet import build_graph as B
+    from fleet import mk
+    from fleet.capture import softmax_scale
+    from fleet.graph_plan import partials_row
+    bw, kind = peaks()
+    nh, d_r, d_c, d_v = 16, 64, 512, 128
+    for ctx in (1024, 4096, 16384, 32768):
+        g = torch.Generator(device="cuda").manual_seed(3)
+        rn = lambda *sh: torch.randn(*sh, generator=g, device="cuda").to(torch.bfloat16)  # noqa: E731
+        ql, qp, ck, kp = rn(nh, d_c), rn(nh, d_r), rn(ctx, d_c), rn(ctx, d_r)
+        W = (torch.randn(nh, d_v, d_c, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+        for n_splits in (8, 16, 32):
+            split = -(-ctx // n_splits)
+            for form in ("tc", "exact"):
+                if form == "exact" and split > 168:
+                    continue
+                partials = torch.zeros((n_splits, nh, partials_row(d_c)), dtype=torch.float32, device="cuda")
+                attn = torch.zeros(nh * d_v, dtype=torch.bfloat16, device="cuda")
+                k = mk.MegaKernel(0)
+                k.add(B.mla_attend_layer(mk, None, ql, qp, ck, kp, partials, softmax_scale(128, d_r), split, n_splits,
+                                         nh if form == "tc" else 1, tc=form == "tc",
+                                         col_parts=4 if form == "tc" and n_splits <= 16 else 1))
+                k.add(B.mla_merge_uv_layer(mk, None, partials, W, attn, split, n_splits))
+                k.finalize()
+                t = _time_kernel(torch, k, ctx - 2, args.steps, args.warmup)
+                k.close()
+                us = sum(t) / len(t)
+                algo = ctx * (d_c + d_r) * 2 + nh * (d_c + d_r) * 2 + nh * d_v * d_c * 2
+                print(json.dumps({"metric": "MLA decode attention us/call (C2)", "value": round(us, 2), "unit": "us",
+                                  "higher_is_better": False, "config": {"workload": "C2", "ctx": ctx,
+                                  "n_splits": n_splits, "split_rows": split, "form": form},
+                                  "steps": args.steps, "warmup": args.warmup, "l2": "flushed between launches",
+                                  "roofline": {"bound": "hbm", "achieved": round(algo / us / 1e3, 1), "peak": bw,
+                                               "unit": "GB/s", "frac": round(algo / us / 1e3 / bw, 4),
+                                               "peak_kind": kind, "algorithmic_bytes": algo},
+                                  "flops": 2 * nh * ctx * (d_c + d_r + d_c)}))
+
+
+def run_c0(args):
+    """Config 0: one MoE decoder layer (layer index 1) of the DeepSeek-V2-Lite shape at position 1024,
+    seeded weights, hidden ~N(0,1), 1024 cached rows ~N(0,1) (seed 1): its nine operators in one
+    launch, x_res restored before each (outside the timed region)."""
+    import torch
     from fleet import build_graph as B
     from fleet import graph_plan as G
-    d = REAL_DIMS
-    s_max = N_PROMPT + 4
-    layers = 3
-    packed = synthetic_packed(d, layers=layers, head=True, seed=0, device=device)
-    capture = make_capture(d, layers, s_max, N_PROMPT - 1, seed=1, device=device)
-    prompt = torch.randint(0, d.V, (N_PROMPT,), generator=torch.Generator().manual_seed(2)).tolist()
-    meta = B.make_meta(torch, s_max, prompt, N_PROMPT, device=device)
-    plan = G.build_plan(d, s_max, layers, True)
-    vals = []
-    for _ in range(max(1, min(args.steps, 1))):
-        cpu = cpu_baseline(packed, capture, meta, d, plan, args.cpu_sample_s)
-        vals.append(cpu["value"])
-    v = sum(vals) / len(vals)
-    out = {"metric": METRIC, "value": round(v, 2), "unit": "ms/token", "n_gpus": ws, "steps": len(vals),
-           "warmup": 0, "ms_per_step": round(v, 2), "higher_is_better": False, "impl": "reference",
-           "vs_baseline": None, "dtype": "bf16 weights, FP32 sums in the specified orders (oracle port)", "data": "synthetic",
-           "config": {"workload": "C1: 27-layer DeepSeek-V2-Lite-shaped greedy decode, batch 1 (CPU oracle port)"},
-           "cpu_baseline": {"value": round(v, 2), "unit": "ms/token", "cores": cpu["cores"], "kind": "port",
-                            "sample": cpu["sample"]},
-           "e2e": {"value": round(v, 2), "unit": "ms/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(out))
+    from fleet.capture import make_capture
+    from fleet.pack_weights import REAL_DIMS as d
+    from fleet.pack_weights import moe_layer_bytes, synthetic_packed
+    bw, kind = peaks()
+    s_max, pos = 1056, 1024
+    packed = synthetic_packed(d, layers=2, head=False, seed=0, device="cuda")
+    capture = make_capture(d, 2, s_max, pos, seed=1, device="cuda")
+    meta = B.make_meta(torch, s_max, [0] * (pos + 1), pos + 1)
+    for form in ("exact", "tc"):
+        plan = G.build_plan(d, s_max, 2, False, attend_tc=form == "tc")
+        plan.calls = [c for c in plan.calls if c.label.startswith("L1.")]
+        mpk, host, plan = B.build(packed, capture, meta, dims=d, s_max=s_max, layers=2, head=False, plan=plan)
+        mpk.compile()
+        x0 = torch.randn(d.H, generator=torch.Generator(device="cuda").manual_seed(7), device="cuda").to(torch.bfloat16)
+        t = _time_kernel(torch, mpk.kernel, pos - 1, args.steps, args.warmup,
+                         before=lambda: host["x_res"][0].copy_(x0))
+        mpk.kernel.close()
+        us = sum(t) / len(t)
+        algo = moe_layer_bytes(d, ctx=pos + 1)
+        print(json.dumps({"metric": "one MoE decoder layer us/step (C0)", "value": round(us, 2), "unit": "us",
+                          "higher_is_better": False, "config": {"workload": "C0: layer 1 at position 1024",
+                          "attention": form, "ops": plan.n_ops}, "steps": args.steps, "warmup": args.warmup,
+                          "l2": "flushed between launches",
+                          "roofline": {"bound": "hbm", "achieved": round(algo / us / 1e3, 1), "peak": bw, "unit": "GB/s",
+                                       "frac": round(algo / us / 1e3 / bw, 4), "peak_kind": kind,
+                                       "algorithmic_bytes": algo}}))
 
 
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "c2":
+        run_c2(args)
+    elif args.config == "c0":
+        run_c0(args)
     else:
         run_ours(args)
 
