@@ -918,22 +918,38 @@ __device__ __forceinline__ void attend_pairs(const KernelParams& P, Smem& sm, co
 // past the split are read from an own-row buffer and a zero chunk instead of the ring. FP32
 // accumulation in the tensor cores' order, so the partials agree with the specified-order path
 // within rounding, not bit for bit.
-// shared address of column c (a multiple of 8) of slot r (0..23) of the stage at sb
-__device__ __forceinline__ uint32_t tc_swz(uint32_t sb, int r, int c) {
-  const int box = c >> 6, chunk = (c & 63) >> 3;
-  return sb + (uint32_t)(box * TC_BOX + r * 128 + ((chunk ^ (r & 7)) << 4));
-}
+struct TcRow {      // one row of a chunk: the shared address of its column c is
+  uint32_t base;     //   base + (c >> 6) * box + ((((c & 63) >> 3) ^ key) << 4 & mask)
+  uint32_t box, key, mask;
+  __device__ __forceinline__ uint32_t at(int c) const {
+    return base + (uint32_t)(c >> 6) * box + (((((uint32_t)c & 63u) >> 3) ^ key) << 4 & mask);
+  }
+};
 struct TcRows {    // where a chunk's rows are: nt streamed rows in ring stages from index idx0
   uint32_t ring0, own, zero;
   int idx0, nt, own_r;
-  __device__ __forceinline__ uint32_t at(int r, int c) const {
-    if (r < nt) {
+  __device__ __forceinline__ TcRow row(int r) const {
+    TcRow w;
+    if (r < nt) {              // a swizzled stage row: 64-column boxes of TC_BOX bytes
       const int st = r / TC_RPS, slot = r - st * TC_RPS;
       int idx = idx0 + st;
       idx -= idx >= NSTAGES ? NSTAGES : 0;
-      return tc_swz(ring0 + (uint32_t)idx * STAGE_BYTES, slot, c);
+      w.base = ring0 + (uint32_t)idx * STAGE_BYTES + (uint32_t)slot * 128u;
+      w.box = TC_BOX;
+      w.key = (uint32_t)(slot & 7);
+      w.mask = 0xFFFFFFFFu;
+    } else if (r == own_r) {   // the own row, unswizzled: 128 bytes per 64 columns
+      w.base = own;
+      w.box = 128u;
+      w.key = 0u;
+      w.mask = 0xFFFFFFFFu;
+    } else {                   // past the chunk: one zero chunk
+      w.base = zero;
+      w.box = 0u;
+      w.key = 0u;
+      w.mask = 0u;
     }
-    return r == own_r ? own + (uint32_t)c * 2u : zero;
+    return w;
   }
 };
 
@@ -1006,7 +1022,8 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
     const int pairs = (R + 15) / 16;
     const bool split_k = pairs <= 4;
     const int jp = split_k ? (warp >> 1) : warp, kh = split_k ? (warp & 1) : 0;
-    const int k0 = split_k ? 18 * kh : 0, k1 = split_k ? k0 + 18 : 36;
+    // k-steps in groups of four (one 64-column box each): halves of 5 and 4 groups when split
+    const int g0 = split_k ? 5 * kh : 0, g1 = split_k ? (kh ? 9 : 5) : 9;
     float mx_g = NEG_INF, mx_g8 = NEG_INF;
     float acc[2][4];
     const bool in_pair = jp < pairs;
@@ -1016,19 +1033,27 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[0][i] = acc[1][i] = accb[0][i] = accb[1][i] = 0.0f;
       const int qh = (lane & 7) + 8 * ((lane >> 3) & 1), qk = 8 * (lane >> 4);
-      const int br = 16 * jp + (lane & 7) + 8 * (lane >> 4), bk = 8 * ((lane >> 3) & 1);
+      const int bk = 8 * ((lane >> 3) & 1);
+      const TcRow kr = tr.row(16 * jp + (lane & 7) + 8 * (lane >> 4));
+      uint32_t off[4];   // the lane's column offsets within a box for the four k-steps of a group
+#pragma unroll
+      for (int j = 0; j < 4; ++j) off[j] = (((uint32_t)(2 * j) + (uint32_t)(bk >> 3)) ^ kr.key) << 4 & kr.mask;
       const uint32_t qa = qbase + (uint32_t)(qh * TC_QSTRIDE + qk * 2);
-#pragma unroll 2
-      for (int kk = k0; kk < k1; kk += 2) {
-        uint32_t a0, a1, a2, a3, b0, b1, b2, b3, e0, e1, e2, e3, f0, f1, f2, f3;
-        ldsm_x4(qa + (uint32_t)kk * 32u, a0, a1, a2, a3);
-        ldsm_x4(tr.at(br, 16 * kk + bk), b0, b1, b2, b3);
-        ldsm_x4(qa + (uint32_t)(kk + 1) * 32u, e0, e1, e2, e3);
-        ldsm_x4(tr.at(br, 16 * (kk + 1) + bk), f0, f1, f2, f3);
-        mma_bf16_16816(acc[0], a0, a1, a2, a3, b0, b1);
-        mma_bf16_16816(acc[1], a0, a1, a2, a3, b2, b3);
-        mma_bf16_16816(accb[0], e0, e1, e2, e3, f0, f1);
-        mma_bf16_16816(accb[1], e0, e1, e2, e3, f2, f3);
+#pragma unroll 1
+      for (int gi = g0; gi < g1; ++gi) {
+        const uint32_t kb = kr.base + (uint32_t)gi * kr.box, qg = qa + (uint32_t)gi * 128u;
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+          uint32_t a0, a1, a2, a3, b0, b1, b2, b3, e0, e1, e2, e3, f0, f1, f2, f3;
+          ldsm_x4(qg + (uint32_t)j * 32u, a0, a1, a2, a3);
+          ldsm_x4(kb + off[j], b0, b1, b2, b3);
+          ldsm_x4(qg + (uint32_t)(j + 1) * 32u, e0, e1, e2, e3);
+          ldsm_x4(kb + off[j + 1], f0, f1, f2, f3);
+          mma_bf16_16816(acc[0], a0, a1, a2, a3, b0, b1);
+          mma_bf16_16816(acc[1], a0, a1, a2, a3, b2, b3);
+          mma_bf16_16816(accb[0], e0, e1, e2, e3, f0, f1);
+          mma_bf16_16816(accb[1], e0, e1, e2, e3, f2, f3);
+        }
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -1136,12 +1161,13 @@ __device__ __noinline__ void attend_tc(const KernelParams& P, Smem& sm, const Op
       for (int kk = 0; kk < pairs; ++kk) {
         uint32_t a0, a1, a2, a3;
         ldsm_x4(pbase + (uint32_t)(ph * TC_PSTRIDE + (16 * kk + pk) * 2), a0, a1, a2, a3);
+        const TcRow vrow = tr.row(16 * kk + vr);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int pi = warp + 8 * i;
           if (pi < npairs) {
             uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(tr.at(16 * kk + vr, vc + 16 * pi), b0, b1, b2, b3);
+            ldsm_x4_t(vrow.at(vc + 16 * pi), b0, b1, b2, b3);
             mma_bf16_16816(o[2 * i], a0, a1, a2, a3, b0, b1);
             mma_bf16_16816(o[2 * i + 1], a0, a1, a2, a3, b2, b3);
           }

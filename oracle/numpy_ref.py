@@ -22,6 +22,7 @@ from oracle.detmath import (F32, F64, _od, bf16, block_sum, butterfly, det_exp, 
                             seq_sum, silu, vals)
 
 __all__ = ["bf16", "rmsnorm", "rope", "mla_prep", "mla_attend", "merge_partials", "mla_merge_uv",
+           "attention_decompressed",
            "moe_router", "moe_router_norm", "moe_w13", "moe_w2", "silu", "linear", "linear_norm",
            "linear_residual", "moe_combine", "dense_mlp", "embed", "lm_head_argmax",
            "partials_row", "softmax_det"]
@@ -199,6 +200,26 @@ def mla_merge_uv(partials, W_uv, step, *, split=32, d_c=None):
     W_uv = np.asarray(W_uv)
     attn = np.stack([dot_rows(W_uv[h], o[h]) for h in range(W_uv.shape[0])])
     return bf16(attn.reshape(-1))
+
+
+def attention_decompressed(q_nope, q_pe, c_kv, k_pe, W_uk, W_uv, step, softmax_scale):
+    """The model's own attention order for the same token, with the keys and values decompressed
+    (harness/numpy_ref.py:187-198, restated): k_nope = bf16(W_uk c) and v = bf16(W_uv c) per
+    position (BF16 like the model's kv_b_proj output), scores q_nope . k_nope + q_pe . k_pe in FP32,
+    scaled and rounded to BF16 (the model's attn_weights), an FP32 softmax rounded to BF16, then
+    bf16(P v). It bounds the error of the absorbed form (scores against the latent, W_uv after the
+    merge), which reassociates these products. Returns (attn [nh * d_v], scores [nh, step + 1])."""
+    c = vals(c_kv)[:step + 1].astype(F32)
+    W_uk, W_uv = vals(W_uk), vals(W_uv)
+    k_nope = bf16(np.einsum("hnc,sc->hsn", W_uk, c, dtype=F32, optimize=True))
+    v = bf16(np.einsum("hvc,sc->hsv", W_uv, c, dtype=F32, optimize=True))
+    s = np.einsum("hn,hsn->hs", vals(q_nope), k_nope, dtype=F32, optimize=True)
+    s = (s + vals(q_pe) @ vals(k_pe)[:step + 1].T).astype(F32)
+    s = bf16((s * F32(softmax_scale)).astype(F32))
+    e = np.exp((s - s.max(axis=-1, keepdims=True)).astype(F32)).astype(F32)
+    p = bf16((e / e.sum(axis=-1, keepdims=True)).astype(F32))
+    out = np.einsum("hs,hsv->hv", p, v, dtype=F32, optimize=True)
+    return bf16(out.reshape(-1)), s
 
 
 # ---------------------------------------------------------------------------------------------

@@ -130,8 +130,10 @@ def test_c1_tensor_core_attention_agrees_up_to_near_ties(c1):
     * routes: before the first id divergence, a mismatch must be one expert swapped for one whose
       oracle router probability is within TIE_REL of the larger (a tie), or come after such a tie
       (a cascade), as compare_route_log classifies them (:181-236);
-    * every cache row appended before the divergence within 2e-2 of the oracle's (rel_err, the L2
-      norm of the difference over the oracle row's: the reference's boundary metric).
+    * every cache row appended before the divergence within 5e-2 of the oracle's (rel_err, the L2
+      norm of the difference over the oracle row's: the reference's boundary metric, at its
+      threshold for a layer's output, harness/common.py:28-40; a row at step t of layer l carries
+      the rounding differences of every earlier layer and step).
     The exact form (the default) is the one whose 32 ids equal the oracle's; this form is the
     tensor-core alternative and states how far it agrees."""
     from oracle.detmath import from_bf16_bits
@@ -163,7 +165,7 @@ def test_c1_tensor_core_attention_agrees_up_to_near_ties(c1):
         rel = np.linalg.norm(g - o, axis=1) / np.maximum(np.linalg.norm(o, axis=1), 1e-30)
         if rel.size:
             worst = max(worst, float(rel.max()))
-            assert rel.max() <= 2e-2, f"{k}: cache rows differ by rel_err {rel.max():.3g}"
+            assert rel.max() <= 5e-2, f"{k}: cache rows differ by rel_err {rel.max():.3g}"
     print(f"c1 tensor cores: ids equal for {first} of {ITERS} steps"
           + (f" (the oracle's top-2 gap at step {first}: {c1['margins'][first]['gap']:.3g})" if first < ITERS else "")
           + f"; route ties {ties}, cascades {cascades}; worst cache row {worst:.3g}")
