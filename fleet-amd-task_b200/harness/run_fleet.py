@@ -233,7 +233,8 @@ def main(argv=None):
         save_file({"hidden": hidden.contiguous()}, str(out / "fleet_hidden_per_layer.safetensors"))
     if "route_log" in host:
         rl = host["route_log"].cpu()
-        n_moe = max(0, args.layers - 1)
+        # the MoE layers whose router is in the plan (a --stop-after plan ends before the rest)
+        n_moe = sum(1 for c in pj["calls"] if c["label"].endswith(".router"))
         log = [[{"idx": rl[s % rl.shape[0], j].tolist(), "w": []} for j in range(n_moe)] for s in range(args.iters)]
         (out / "fleet_route_log.json").write_text(json.dumps(log) + "\n")
     wall = {"mpk_wall_s": t_run, "iters": args.iters, "pack_s": t_pack, "build_s": t_build}

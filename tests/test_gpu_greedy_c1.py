@@ -117,39 +117,87 @@ def test_c1_27_layers_32_greedy_tokens_one_launch_match_oracle(c1):
     print(f"c1 exact: 32 greedy ids equal the oracle's ({c1['oracle_s']:.0f} s of oracle); ids {got['ids']}")
 
 
-def test_c1_tensor_core_attention_within_tolerance(c1):
-    """The same decode with the MLA attention on the tensor cores (FP32 accumulation in the tensor
-    cores' order, so every attention output differs from the specified-order one in the last bits
-    and the differences compound over 27 layers and 32 steps). Step 0 starts from the oracle's
-    state, so it is held to the north-star tolerance: every cache row it appends within 2e-2 of
-    the oracle's (rel_err, the reference's boundary metric), every routed-expert choice equal or a
-    tie by the reference's rule (one expert swapped for one whose oracle probability is within 2e-2
-    of the larger, harness/compare.py:181-236), the first token equal. Later steps decode from the
-    form's own state: how many ids still match is reported, not required (on this random-weight
-    model near-ties make greedy ids fragile under any change of summation order; the exact form,
-    the default, matches all 32)."""
+def max_abs_rel(g, o):
+    """max |g - o| / max |o| (the per-layer-output metric the tolerance is stated in)."""
+    g, o = np.asarray(g, np.float64), np.asarray(o, np.float64)
+    return float(np.abs(g - o).max() / max(np.abs(o).max(), 1e-30))
+
+
+def test_c1_tensor_core_attention_per_layer_tolerance(c1):
+    """The same model with the MLA attention on the tensor cores (FP32 accumulation in the tensor
+    cores' order: every attention output differs from the specified-order one in the last bits).
+    Each layer is held to the tolerance on the input the kernel gave it: one decode step with the
+    per-layer residual snapshots (the reference's debug graph) and, per layer l, the oracle's layer l
+    applied to the kernel's layer l - 1 output. Then, per layer:
+      * the latent-cache row it appends equals the oracle's bit for bit (norm1, q/kv_a and the prep
+        come before the attention);
+      * the routed experts equal the oracle's, or differ by one tie under the reference's rule
+        (harness/compare.py:181-236: the two probabilities within 2e-2 of the larger);
+      * the layer output is within max-abs relative error 2e-2 of the oracle's (where the routes
+        are equal);
+    and the head's logits and token equal the oracle's on the kernel's last residual.
+    A 32-step decode then runs from the form's own state; how many ids stay equal to the exact
+    oracle's is printed, not required: on this random-weight model the residual stream amplifies
+    any difference layer over layer, and near-ties make later greedy ids fragile under any change
+    of summation order (the exact form, the default, matches all 32)."""
+    from fleet import build_graph as B
+    from fleet.capture import softmax_scale
+    from fleet.graph_plan import SPLIT
     from oracle.detmath import from_bf16_bits
+    w = c1["w"]
+    d = w.dims
+    pos = w.first_pos
+    for k, v in c1["cache0"].items():
+        w.capture[k].view(torch.int16).copy_(torch.from_numpy(v.view(np.int16)))
+    meta = B.make_meta(torch, w.s_max, w.prompt, w.n_prompt, device=DEV)
+    mpk, host, plan = B.build(w.packed, w.capture, meta, dims=d, s_max=w.s_max, layers=d.L, head=True, debug=True,
+                              attend_tc=True)
+    mpk.compile()
+    mpk.launch(1)
+    torch.cuda.synchronize()
+    st = mpk.status()
+    assert st["error"] == 0 and st["generation"] == 1, st
+    xs = [from_bf16_bits(u16(host[f"dbg_x_res_{l}"][0])) for l in range(d.L)]
+    rows = {k: u16(w.capture[k])[pos].copy() for k in c1["cache0"]}
+    routes = host["route_log"].cpu().numpy()[0]
+    logits = u16(host["logits"][0])
+    token = int(meta["tokens"][0, pos + 1])
+    mpk.kernel.close()
+
+    dw = DeviceWeightBits(w.packed, keep_experts=range(d.E, d.E_TOTAL))
+    m = OracleModel(d, dw.get, dw.get_expert, softmax_scale=softmax_scale(d.D_N, d.D_R), split=SPLIT)
+    cache = {k: from_bf16_bits(v).copy() for k, v in c1["cache0"].items()}
+    cos, sin = (w.capture[k].float().cpu().numpy() for k in ("cos", "sin"))
+    x_in = R.embed(dw.get("W_embed"), int(meta["tokens"][0, pos]))
+    worst, ties = (0.0, -1), 0
+    for l in range(d.L):
+        rec = {}
+        xa = m.attention(l, x_in, cache, cos, sin, pos, rec)
+        out = m.dense_mlp(xa, rec) if l == 0 else m.moe(l, xa, rec)
+        for k in (f"c_kv_{l}", f"k_pe_{l}"):
+            assert np.array_equal(rows[k], bf16_bits(cache[k][pos])), f"{k}: the appended row differs"
+        same_route = True
+        if l >= 1:
+            r, f = sorted(rec[f"L{l}.mask"][:d.TOPK].tolist()), sorted(routes[l - 1, :d.TOPK].tolist())
+            if r != f:
+                gone, new = sorted(set(r) - set(f)), sorted(set(f) - set(r))
+                p = R.softmax_det(rec[f"L{l}.router_logits"])
+                assert len(gone) == 1 and abs(float(p[gone[0]]) - float(p[new[0]])) <= \
+                    2e-2 * max(p[gone[0]], p[new[0]]), f"layer {l}: routes {f} vs {r} is no tie"
+                ties += 1
+                same_route = False
+        if same_route:
+            e = max_abs_rel(xs[l], out)
+            assert e <= 2e-2, f"layer {l}: output max-abs relative error {e:.3g}"
+            worst = max(worst, (e, l))
+        x_in = xs[l]                 # the next layer starts from the kernel's output
+    h, ologits, otok = R.lm_head_argmax(xs[-1], dw.get("w_final_norm"), dw.get("W_lm"))
+    assert np.array_equal(logits, bf16_bits(ologits)) and token == otok
+
     got = run_c1(c1, attend_tc=True)
-    pos0, d = c1["w"].first_pos, c1["w"].dims
-    worst = 0.0
-    for k, v in got["cache"].items():
-        g = from_bf16_bits(v[pos0]).astype(np.float64)
-        o = c1["ocache"][k][pos0].astype(np.float64)
-        rel = float(np.linalg.norm(g - o) / max(np.linalg.norm(o), 1e-30))
-        worst = max(worst, rel)
-        assert rel <= 2e-2, f"{k}: the step-0 cache row differs by rel_err {rel:.3g}"
-    ties = 0
-    for j in range(d.L - 1):
-        r, f = sorted(c1["routes"][0][j]), sorted(got["route_log"][0, j, :d.TOPK].tolist())
-        if r != f:
-            gone, new = sorted(set(r) - set(f)), sorted(set(f) - set(r))
-            p = c1["margins"][0]["probs"][j + 1]
-            assert len(gone) == 1 and abs(float(p[gone[0]]) - float(p[new[0]])) <= 2e-2 * max(p[gone[0]], p[new[0]]), \
-                f"MoE layer {j + 1}: routes {f} vs {r} at step 0 is no tie"
-            ties += 1
-    assert got["ids"][0] == c1["ids"][0]
     first = next((i for i in range(ITERS) if got["ids"][i] != c1["ids"][i]), ITERS)
-    print(f"c1 tensor cores: step 0 within tolerance (worst cache row rel_err {worst:.3g}, {ties} route ties); "
-          f"ids equal for {first} of {ITERS} steps"
+    print(f"c1 tensor cores: per-layer max-abs relative error at most {worst[0]:.3g} (layer {worst[1]}), "
+          f"{ties} route ties, cache rows and head exact on the kernel's inputs; a 32-step decode from "
+          f"its own state keeps the oracle's ids for {first} of {ITERS} steps"
           + (f" (the oracle's top-2 logit gap at step {first}: {c1['margins'][first]['gap']:.3g} of the largest)"
              if first < ITERS else ""))
