@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--attend", default="exact", choices=["exact", "tc"],
                     help="MLA attention form: the bit-exact FP32 CUDA-core tasks, or the tensor-core tasks")
     ap.add_argument("--split", type=int, default=None, help="cache rows per attention split (default: the plan's)")
+    ap.add_argument("--moe", default=None, choices=["units", "staged"],
+                    help="the experts' form (default: units on one GPU; expert parallelism is staged)")
     ap.add_argument("--tc-parts", type=int, default=1, help="tensor-core attention: latent-column parts per split")
     ap.add_argument("--op-tasks", default="", help="task counts per operator kind, e.g. router=16,qkva=96")
     ap.add_argument("--trace", action="store_true",
@@ -208,7 +210,8 @@ def build_model(args, device, layers, ep=None):
     extra = {} if args.split is None else dict(split=args.split)
     mpk, host, plan = B.build(packed, capture, meta, dims=d, s_max=s_max, layers=layers, head=True,
                               trace=args.trace, ep=ep, logit_bias=routing != "natural",
-                              attend_tc=args.attend == "tc", tc_parts=args.tc_parts, op_tasks=op_tasks(args), **extra)
+                              attend_tc=args.attend == "tc", tc_parts=args.tc_parts, op_tasks=op_tasks(args),
+                              moe=args.moe, **extra)
     mpk.compile()
     torch.cuda.synchronize()
     build_model.workload = w
@@ -496,7 +499,7 @@ def run_ours(args):
                    "l2": "no flush: 4.9 GB read per step >> 126 MB L2", "routing": args.routing,
                    "attention": ("tensor cores (mma.sync BF16, FP32 accumulation)" if args.attend == "tc" else
                                  "FP32 CUDA cores, specified summation order (bit-exact)"),
-                   "split": plan.split, "tc_parts": args.tc_parts if args.attend == "tc" else None,
+                   "split": plan.split, "moe": plan.moe, "tc_parts": args.tc_parts if args.attend == "tc" else None,
                    "op_tasks": op_tasks(args),
                    "tokens_per_s": round(1e3 / ms, 2)},
         "tokens_per_s": round(1e3 / ms, 2),

@@ -161,6 +161,49 @@ __device__ bool produce_task(const KernelParams& P, Smem& sm, Prod& pr, const Op
       }
       return true;
     }
+    case MK_OP_MOE_UNITS: {
+      // per unit: its lanes' gate/up rows (16 per lane: intermediates 8 l .. 8 l + 7 of the part,
+      // gate and up interleaved), then its rows of the regrouped down projection. The fixed
+      // slots' units first; the routed slots' units once the router has written the expert ids.
+      const int H = (int)I_(od, MK_I_MU_H), I = (int)I_(od, MK_I_MU_I);
+      const int KP = unit_parts(I), Lp = I / KP, l8 = Lp / 8, slot0 = (int)I_(od, MK_I_MU_SLOT0);
+      const int fixed0 = (int)I_(od, MK_I_MU_FIXED0), nexp = (int)I_(od, MK_I_MU_NEXP), r13 = unit_w13_rows(H);
+      const uint8_t* W13 = P_<const uint8_t>(od, MK_P_MU_W13);
+      const uint8_t* W2F = P_<const uint8_t>(od, MK_P_MU_W2F);
+      const int32_t* mask = P_<const int32_t>(od, MK_P_MU_MASK);
+      const MuList ml = mu_list(t);
+      for (int v = 0; v < ml.nf + ml.nr; ++v) {
+        if (v == ml.nf && od.aux[0] >= 0) {   // the first routed unit: wait for this iteration's router
+          const OpDev& dep = P.ops[od.aux[0]];
+          if (!wait_event(P, sm, &P.events[od.aux[0]], (uint32_t)dep.ntasks * itx.g, false)) {
+            report_error(P, sm, *(volatile uint32_t*)&P.status->abort_flag ? MK_DERR_ABORTED : MK_DERR_WAIT_TIMEOUT,
+                         op, task, 0x10000u | (uint32_t)od.aux[0]);
+            return false;
+          }
+          fence_proxy_async_global();
+        }
+        {
+          const int u = P.units[ml.off + v];
+          const int s = slot0 + u / (KP * 8), pt = (u >> 3) % KP, q = u & 7, nl = unit_lanes(q, l8);
+          const int e = s >= fixed0 ? (int)I_(od, MK_I_MU_EXP0) + (s - fixed0) : __ldcg(mask + s);
+          if (e < 0 || e >= nexp) { report_error(P, sm, MK_DERR_BAD_EXPERT, op, task, (uint32_t)e); return false; }
+          const uint8_t* w13 = W13 + (size_t)e * 2 * I * H * 2;
+          for (int j = 0; j < nl; ++j) {
+            const size_t row0 = 2 * (size_t)(pt * Lp + 8 * (q + 8 * j));
+            for (int r = 0; r < 16; r += r13)
+              if (!issue_stage(P, sm, pr, w13 + (row0 + r) * H * 2, (uint32_t)(r13 * H * 2), nullptr, 0, 0, op, task))
+                return false;
+          }
+          const uint8_t* w2 =
+              W2F + ((size_t)e * H * I + (size_t)pt * H * Lp + (size_t)H * unit_q_vals(q, l8)) * 2;
+          const int rb = 16 * nl, r2 = STAGE_BYTES / rb;
+          for (int r = 0; r < H; r += r2)
+            if (!issue_stage(P, sm, pr, w2 + (size_t)r * rb, (uint32_t)(min(r2, H - r) * rb), nullptr, 0, 0, op, task))
+              return false;
+        }
+      }
+      return true;
+    }
     case MK_OP_MLA_ATTEND: {
       const AttSplit a = att_split(od, t, itx.pos);
       if (od.op.flags & MK_F_TC) {   // TMA boxes of 24 rows, in chunks of TC_CHUNK rows
@@ -1568,6 +1611,149 @@ __device__ void w2_body(const KernelParams& P, Smem& sm, const OpDev& od, const 
   }
 }
 
+// ---- expert units: gate/up, SwiGLU and the down projection's subtree sums ----------------------
+// A task runs its range of units (slot s, part p, lane class q). Per unit: the gate/up rows of
+// its intermediates through the row engine (the GATEUP arithmetic: BF16 gate and up, act =
+// bf16(silu(gate) up)), then, one row per thread, each of its lanes' down-projection value
+// (even products + odd products, the row engine's lane value) and the two butterfly levels over
+// the class: S_q = (v_q + v_(q+16)) + (v_(q+8) + v_(q+24)), +0 for lanes without values.
+template <int KS>
+__device__ void moe_units_body(const KernelParams& P, Smem& sm, const OpDev& od, const TaskDev& t, const Iter& itx,
+                               Cons& c) {
+  const int H = (int)I_(od, MK_I_MU_H), I = (int)I_(od, MK_I_MU_I);
+  const int KP = unit_parts(I), Lp = I / KP, l8 = Lp / 8, slot0 = (int)I_(od, MK_I_MU_SLOT0);
+  const int r13 = unit_w13_rows(H);
+  uint4 xv;
+  if (od.op.flags & MK_F_NORM) {
+    uint16_t* hbuf = xbuf_of(sm);
+    rmsnorm_to_smem(P_<const uint16_t>(od, MK_P_MU_X), P_<const uint16_t>(od, MK_P_MU_WNORM), H, (float)od.op.fp[0],
+                    hbuf, sm, c);
+    uint16_t* hout = P_<uint16_t>(od, MK_P_MU_HOUT);
+    if (hout && t.idx == 0)
+      for (int i = c.tid; i < H; i += NUM_CONSUMERS) hout[i] = hbuf[i];
+    xv = x_part<KS, true>(hbuf, H, c);
+  } else {
+    xv = x_part<KS, false>(P_<const uint16_t>(od, MK_P_MU_X), H, c);
+  }
+  (void)itx;
+  mark_body(sm, c);
+  float* pbuf = pbuf_of(sm);
+  uint16_t* abuf = reinterpret_cast<uint16_t*>(sm.scratch + MU_ABUF_OFF);
+  float* sums = P_<float>(od, MK_P_MU_SUMS);
+  uint16_t* actg = P_<uint16_t>(od, MK_P_MU_ACT);
+  const MuList ml = mu_list(t);
+  for (int v = 0; v < ml.nf + ml.nr; ++v) {   // the fixed slots' units, then the routed slots'
+    const int u = P.units[ml.off + v];
+    const int s = slot0 + u / (KP * 8), pt = (u >> 3) % KP, q = u & 7, nl = unit_lanes(q, l8);
+    for (int j = 0; j < nl; ++j)
+      for (int r = 0; r < 16; r += r13) {
+        const uint8_t* stg = acquire_stage(P, sm, c, (uint32_t)t.op, (uint32_t)t.idx);
+        stage_parts<KS>(stg, r13, H, 16 * j + r, pbuf, c, [&](int) { return xv; });
+        release_stage(sm, c);
+      }
+    consumer_sync();
+    if (c.tid < 8 * nl) {   // intermediate 8 (q + 8 j) + k of the part: local rows 16 j + 2 k (gate), + 1 (up)
+      const int j = c.tid >> 3, k = c.tid & 7;
+      const uint32_t gb = f32_to_bf16_bits(row_total<KS>(pbuf, 16 * j + 2 * k, ks_of<KS>(H)));
+      const uint32_t ub = f32_to_bf16_bits(row_total<KS>(pbuf, 16 * j + 2 * k + 1, ks_of<KS>(H)));
+      const uint32_t ab = f32_to_bf16_bits(__fmul_rn(det_silu(bf16_bits_to_f32(gb)), bf16_bits_to_f32(ub)));
+      abuf[c.tid] = (uint16_t)ab;
+      if (actg) actg[(size_t)s * I + pt * Lp + 8 * (q + 8 * j) + k] = (uint16_t)ab;
+    }
+    consumer_sync();
+    const uint32_t ab0 = smem_u32(abuf);
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    const uint4 x0 = lds128(ab0), x1 = nl > 1 ? lds128(ab0 + 16u) : z, x2 = nl > 2 ? lds128(ab0 + 32u) : z,
+                x3 = nl > 3 ? lds128(ab0 + 48u) : z;
+    float* out = sums + ((size_t)(s * KP + pt) * 8 + q) * H;
+    const int rb = 16 * nl, r2 = STAGE_BYTES / rb;
+    for (int r0 = 0; r0 < H; r0 += r2) {
+      const int nr = min(r2, H - r0);
+      const uint32_t sb = smem_u32(acquire_stage(P, sm, c, (uint32_t)t.op, (uint32_t)t.idx));
+      for (int r = c.tid; r < nr; r += NUM_CONSUMERS) {
+        const uint32_t ra = sb + (uint32_t)(r * rb);
+        auto lane_value = [&](uint32_t a, const uint4& x) {
+          const uint4 w = lds128(a);
+          float a0 = 0.0f, a1 = 0.0f;
+          fma_bf16x2(a0, a1, w.x, x.x);
+          fma_bf16x2(a0, a1, w.y, x.y);
+          fma_bf16x2(a0, a1, w.z, x.z);
+          fma_bf16x2(a0, a1, w.w, x.w);
+          return __fadd_rn(a0, a1);
+        };
+        const float v0 = lane_value(ra, x0);
+        const float v1 = nl > 1 ? lane_value(ra + 16u, x1) : 0.0f;
+        const float v2 = nl > 2 ? lane_value(ra + 32u, x2) : 0.0f;
+        const float v3 = nl > 3 ? lane_value(ra + 48u, x3) : 0.0f;
+        out[r0 + r] = __fadd_rn(__fadd_rn(v0, v2), __fadd_rn(v1, v3));
+      }
+      release_stage(sm, c);
+    }
+  }
+  mark_stages(sm, c);
+}
+
+// ---- expert combine: the down projection per slot from the subtree sums, then x += sum w out8 --
+// One (slot, part, row) per thread for the part sums (the butterfly's last three levels), then
+// one (slot, row) per thread for the parts in order and the BF16 rounding, then the combine of
+// numpy_ref.moe_combine (acc + f32(out * w) in slot order).
+__device__ void moe_combine_body(const KernelParams& P, Smem& sm, const OpDev& od, const TaskDev& t, const Iter& itx,
+                                 Cons& c) {
+  const int H = (int)I_(od, MK_I_MC_H), I = (int)I_(od, MK_I_MC_I), NS = (int)I_(od, MK_I_MC_NS);
+  const int KP = unit_parts(I), l8 = (I / KP) / 8, nr = t.b - t.a;
+  const float* sums = P_<const float>(od, MK_P_MC_SUMS);
+  const float* topk_w = P_<const float>(od, MK_P_MC_TOPKW);
+  uint16_t* xres = P_<uint16_t>(od, MK_P_MC_XRES);
+  uint16_t* out8 = P_<uint16_t>(od, MK_P_MC_OUT8);
+  float* psum = reinterpret_cast<float*>(sm.scratch);       // [NS][KP][nr]
+  float* obs = psum + NS * KP * nr;                          // [NS][nr]
+  float* wk = obs + NS * nr;                                 // [NS]
+  (void)itx;
+  (void)P;
+  if (c.tid < NS) wk[c.tid] = ldcg_f32(topk_w + c.tid);
+  const float res = c.tid < nr ? bf16_bits_to_f32(ldcg_u16(xres + t.a + c.tid)) : 0.0f;
+  mark_body(sm, c);
+  bool live[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) live[q] = unit_lanes(q, l8) > 0;
+  const int n = NS * KP * nr;
+  constexpr int NB = 4;   // four items' loads in flight at a time (one round at the model's sizes)
+  for (int i0 = c.tid; i0 < n; i0 += NB * NUM_CONSUMERS) {
+    float S[NB][8];
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      const int i = i0 + k * NUM_CONSUMERS;
+      const int lr = i % nr, sp = i / nr;
+      const float* src = sums + (size_t)sp * 8 * H + t.a + lr;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) S[k][q] = (i < n && live[q]) ? __ldcg(src + (size_t)q * H) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      const int i = i0 + k * NUM_CONSUMERS;
+      if (i < n)
+        psum[i] = __fadd_rn(__fadd_rn(__fadd_rn(S[k][0], S[k][4]), __fadd_rn(S[k][2], S[k][6])),
+                            __fadd_rn(__fadd_rn(S[k][1], S[k][5]), __fadd_rn(S[k][3], S[k][7])));
+    }
+  }
+  consumer_sync();
+  for (int i = c.tid; i < NS * nr; i += NUM_CONSUMERS) {
+    const int s = i / nr, lr = i - s * nr;
+    float d = psum[(s * KP) * nr + lr];
+    for (int pt = 1; pt < KP; ++pt) d = __fadd_rn(d, psum[(s * KP + pt) * nr + lr]);
+    const uint32_t ob = f32_to_bf16_bits(d);
+    obs[s * nr + lr] = bf16_bits_to_f32(ob);
+    if (out8) out8[(size_t)s * H + t.a + lr] = (uint16_t)ob;
+  }
+  consumer_sync();
+  for (int lr = c.tid; lr < nr; lr += NUM_CONSUMERS) {
+    float acc = lr == c.tid ? res : bf16_bits_to_f32(ldcg_u16(xres + t.a + lr));
+    for (int s = 0; s < NS; ++s) acc = __fadd_rn(acc, __fmul_rn(obs[s * nr + lr], wk[s]));
+    xres[t.a + lr] = (uint16_t)f32_to_bf16_bits(acc);
+  }
+  mark_stages(sm, c);
+}
+
 // ---- stream probe: the ring's bytes, no arithmetic -------------------------------------------
 __device__ void op_stream(const KernelParams& P, Smem& sm, const OpDev& od, const TaskDev& t, const Iter& itx,
                           Cons& c) {
@@ -1651,6 +1837,12 @@ __device__ void run_task(const KernelParams& P, Smem& sm, const OpDev& od, const
     }
     case MK_OP_STREAM: op_stream(P, sm, od, t, itx, c); break;
     case MK_OP_COPY: op_copy(od, c); break;
+    case MK_OP_MOE_UNITS: {
+      const int H = (int)I_(od, MK_I_MU_H);
+      by_parts(H, [&](auto ks) { moe_units_body<decltype(ks)::value>(P, sm, od, t, itx, c); });
+      break;
+    }
+    case MK_OP_MOE_COMBINE: moe_combine_body(P, sm, od, t, itx, c); break;
     default: break;
   }
 }

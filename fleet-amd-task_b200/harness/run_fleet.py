@@ -3,7 +3,7 @@
 
     python harness/run_fleet.py --layers N [--head] [--iters K] [--debug] [--debug-scores]
         [--stop-after L1.o_proj] (--model-dir SNAPSHOT | --synthetic) [--ref REF_DIR] [--out DIR]
-        [--split N] [--attend-tc] [--event-timing] [--align-alloc BYTES] [--workspaces-first]
+        [--split N] [--attend-tc] [--moe units|staged] [--event-timing] [--align-alloc BYTES] [--workspaces-first]
         [the reference's variant switches: --tile-linears ... --merge-oproj, recorded]
 
 The driver of the reference (harness/run_fleet.py:505-616), against this package: positions follow
@@ -95,7 +95,7 @@ def boundary_dump(plan, host, tokens, n_prompt, dims, iters=1):
     if lab:
         if lab.endswith(".o_proj"):
             put(f"L{layer(lab)}.B7.x_res_attn", host["x_res"][0])
-        elif lab.endswith((".w2_combine", ".down")):
+        elif lab.endswith((".w2_combine", ".combine", ".down")):
             put(f"L{layer(lab)}.B13.layer_out", host["x_res"][0])
         elif lab == "prologue.embed":
             put("prologue.embed", host["x_res"][0])
@@ -138,6 +138,7 @@ def build_parser():
     ap.add_argument("--out", required=True)
     ap.add_argument("--split", type=int, default=None, help="cache rows per attention split")
     ap.add_argument("--attend-tc", action="store_true", help="the MLA attention on the tensor cores")
+    ap.add_argument("--moe", default=None, choices=["units", "staged"], help="the experts' form (default: units)")
     ap.add_argument("--event-timing", action="store_true", help="per-task %%globaltimer stamps (event_timing.json)")
     ap.add_argument("--align-alloc", type=int, default=0, help="re-base weights, capture and workspaces on BYTES")
     ap.add_argument("--workspaces-first", action="store_true", help="allocate the workspaces before the weights")
@@ -169,6 +170,7 @@ def main(argv=None):
     variants = {f: getattr(args, f) for f in VARIANT_FLAGS}
     variants.update(linear_grid=args.linear_grid, head_grid=args.head_grid, merge_halves=args.merge_halves)
     kw = {} if args.split is None else dict(split=args.split)
+    kw["moe"] = args.moe
     # the plan's checks run on the dry run, before any weight is packed (the reference's order)
     B.dry_run(dims, s_max, args.layers, args.head, args.debug, args.stop_after, args.debug_scores,
               args.tile_linears, args.attend_tasks, args.fuse_norm2, args.fuse_silu, None, args.fuse_norm1,

@@ -64,16 +64,27 @@ enum MkOpType {
   MK_OP_W2_COMBINE = 8,   /* out8 = W2 act per slot, x += sum w out8     (gang_moe_w2_silu_mi300.cuh
                              + moe_mul_sum_add) */
   MK_OP_STREAM = 9,       /* read-only bandwidth probe of the weight ring (stream_mi300.cuh:99) */
-  MK_OP_COPY = 10         /* dst = src, n BF16 values (the debug per-layer residual snapshot, the
+  MK_OP_COPY = 10,        /* dst = src, n BF16 values (the debug per-layer residual snapshot, the
                              reference's copy_layer in fleet/graph_plan.py:565-567) */
+  MK_OP_MOE_UNITS = 11,   /* the experts' gate/up, SwiGLU and down projection by units: a unit is
+                             (slot, part p of the down projection's K, lane class q mod 8); it
+                             computes the gate/up rows of its intermediates and, for every output
+                             row, the down projection's level-2 butterfly subtree sum over its
+                             lanes (the arithmetic of gang_moe_w13_gemv_mi300.cuh and
+                             gang_moe_w2_silu_mi300.cuh, regrouped) */
+  MK_OP_MOE_COMBINE = 12  /* out8 = bf16(down projection) per slot from the units' subtree sums,
+                             x += sum w out8 (moe_mul_sum_add) */
 };
 
 /* MkOp.flags */
 #define MK_F_NORM (1 << 0)       /* GEMV/GATEUP: RMSNorm prologue on x with ptr w_norm */
 #define MK_F_RESIDUAL (1 << 1)   /* GEMV: add res before the rounding */
 #define MK_F_ARGMAX (1 << 2)     /* GEMV: greedy argmax of the output into tokens[pos + 1] */
-#define MK_F_EXPERT (1 << 3)     /* GATEUP: groups are the routed slots of `mask` */
-#define MK_F_STATIC_IDS (1 << 4) /* GATEUP: `mask` holds constant expert ids (no wait for a router) */
+#define MK_F_EXPERT (1 << 3)     /* GATEUP: groups are the routed slots of `mask`; MOE_UNITS: the
+                                    slots before FIXED0 read their experts from `mask` after the router */
+#define MK_F_STATIC_IDS (1 << 4) /* GATEUP: `mask` holds constant expert ids (no wait for a router);
+                                    MOE_UNITS: slot FIXED0 + k uses expert EXP0 + k (the shared
+                                    experts, no wait for a router) */
 #define MK_F_EP (1 << 5)         /* GATEUP / W2_COMBINE: expert parallelism by slot over N ranks, each
                                     holding every expert's weights: slot s (the TOPK routed slots,
                                     then the shared ones) is computed by rank s mod N. GATEUP spreads
@@ -138,6 +149,30 @@ enum { /* MK_OP_W2_COMBINE */ MK_P_W2_ACT = 0, MK_P_W2_W = 1, MK_P_W2_MASK = 2, 
        MK_I_W2_H = 0, MK_I_W2_I = 1, MK_I_W2_SLOTS = 2, MK_I_W2_ESTRIDE = 3, MK_I_W2_NEXP = 4,
        MK_I_W2_TOPK = 5, MK_I_W2_EPRANK = 6, MK_I_W2_EPWORLD = 7,
        MK_I_W2_LAYER = 8 /* MK_F_EP: the exchange layer, 0 <= layer < MkEpPeers.n_layers */ };
+/* MK_OP_MOE_UNITS. W13 is the packed gate/up tensor [experts][2 I][H] (row 2i gate i, 2i + 1 up i);
+   W2F is the down projection [experts][H][I] regrouped by unit: per expert, per part p (of the
+   KS = parts(I) parts of Lp = I / KS values), per lane class q = 0..7, the rows [H][8 nl(q)] of the
+   values of lanes q, q + 8, q + 16, q + 24 that hold any (nl(q) of them: lane l holds values
+   [p Lp + 8 l, + 8), l < Lp / 8), in that lane order. SUMS [NS][KS][8][H] FP32 receives, per unit and
+   row r, S_q = (v_q + v_(q+16)) + (v_(q+8) + v_(q+24)) with v_l the lane's (even products + odd
+   products) and +0 for a lane that holds no values: the down projection's warp butterfly up to
+   its second level. A q with nl(q) = 0 is no unit (its S_q is +0).
+   The operator covers slots [SLOT0, SLOT0 + NSLOTS): those from FIXED0 on have fixed experts
+   (slot FIXED0 + k: expert EXP0 + k, the shared experts; MK_F_STATIC_IDS), those before FIXED0 take
+   their experts from `mask` after the router (MK_F_EXPERT; the weights stream once the router is
+   done). Every task takes a range of the fixed slots' units and then a range of the routed slots'
+   units, each range about 1/ntasks of its kind's bytes; x (x_res) is normalised by the task itself
+   (MK_F_NORM), so it needs no router output. */
+enum { /* MK_OP_MOE_UNITS */ MK_P_MU_X = 0, MK_P_MU_WNORM = 1, MK_P_MU_W13 = 2, MK_P_MU_W2F = 3, MK_P_MU_MASK = 4,
+       MK_P_MU_SUMS = 5, MK_P_MU_ACT = 6 /* optional [NS][I] BF16 */, MK_P_MU_HOUT = 7 /* optional */,
+       MK_I_MU_H = 0, MK_I_MU_I = 1, MK_I_MU_SLOT0 = 2, MK_I_MU_NSLOTS = 3 /* slots of this operator */,
+       MK_I_MU_NS = 4 /* all slots (SUMS, ACT) */, MK_I_MU_NEXP = 5, MK_I_MU_EXP0 = 6 /* MK_F_STATIC_IDS */,
+       MK_I_MU_FIXED0 = 7 /* the first slot with a fixed expert (SLOT0 + NSLOTS: none) */ };
+/* MK_OP_MOE_COMBINE: per row r and slot s, the down projection's part sums
+   ((S_0 + S_4) + (S_2 + S_6)) + ((S_1 + S_5) + (S_3 + S_7)) added in part order, rounded to BF16
+   (out8), then x_res = bf16(x_res + sum_s f32(out8_s w_s)) in slot order. */
+enum { /* MK_OP_MOE_COMBINE */ MK_P_MC_SUMS = 0, MK_P_MC_TOPKW = 1, MK_P_MC_XRES = 2, MK_P_MC_OUT8 = 3 /* optional */,
+       MK_I_MC_H = 0, MK_I_MC_I = 1, MK_I_MC_NS = 2 };
 /* Expert parallelism: where each rank's exchange words are, as this rank maps them (peer pointers
    opened with mk_ep_ipc_open). xch[r] is rank r's [2][n_layers][n_slots][hidden / 2] array of
    64-bit words: the low half holds two BF16 outputs (rows 2k, 2k + 1 of one slot), the high half

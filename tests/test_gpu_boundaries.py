@@ -45,25 +45,27 @@ CHECKS = {   # label suffix -> [(workspace, record key, slice)]
     "w13s": [("act8", None, None)],
     "w13r": [("act8", None, None)],
     "w2_combine": [("x_res", "layer_out", None), ("out8", "out8", None)],
+    "experts": [("act8", None, None)],
+    "combine": [("x_res", "layer_out", None), ("out8", "out8", None)],
 }
 
 
-@pytest.mark.parametrize("which,split", [("small", 16), ("small", 64)])
-def test_every_boundary(which, split):
+@pytest.mark.parametrize("which,split,moe", [("small", 16, "units"), ("small", 64, "units"), ("small", 16, "staged")])
+def test_every_boundary(which, split, moe):
     from fleet import build_graph as B
     from fleet.pack_weights import Dims
     from oracle import numpy_ref as R
     dims = Dims(**SMALL)
     packed, capture, prompt, s_max, n_past = _setup(dims, split)
     rec = _oracle(dims, packed, capture, prompt, n_past, split)
-    plan = B.G.build_plan(dims, s_max, dims.L, True, split=split)
+    plan = B.G.build_plan(dims, s_max, dims.L, True, split=split, moe=moe)
     labels = [c.label for c in plan.calls]
     failures = []
     for lab in labels:
         cap = {k: v.clone() for k, v in capture.items()}
         meta = B.make_meta(torch, s_max, prompt, n_past + 1, device=DEV)
         mpk, host, plan2 = B.build(packed, cap, meta, dims=dims, s_max=s_max, layers=dims.L, head=True,
-                                   stop_after=lab, split=split)
+                                   stop_after=lab, split=split, moe=moe)
         mpk.compile()
         mpk.step = n_past - 1
         mpk.launch(1)
@@ -89,10 +91,11 @@ def test_every_boundary(which, split):
                 if not np.array_equal(got[:live].view(np.uint32), want[:live].view(np.uint32)):
                     bad = np.nonzero(got[:live] != want[:live])
                     failures.append(f"{lab}: partials differ at {len(bad[0])} places, first {tuple(b[0] for b in bad)}")
-            if op in ("w13s", "w13r"):   # shared slots TOPK.. / routed slots ..TOPK of act8
+            if op in ("w13s", "w13r", "experts"):   # shared slots TOPK.. / routed slots ..TOPK / all of act8
                 mask = rec[f"{prefix}.mask"]
                 act = np.stack([R.swiglu_act(m, dims.I_MOE) for m in rec[f"{prefix}.mid"][:int(mask[-1])]])
-                rows = slice(dims.TOPK, dims.TOPK + dims.N_SHARED) if op == "w13s" else slice(0, dims.TOPK)
+                rows = {"w13s": slice(dims.TOPK, dims.TOPK + dims.N_SHARED), "w13r": slice(0, dims.TOPK),
+                        "experts": slice(0, dims.TOPK + dims.N_SHARED)}[op]
                 if not np.array_equal(np32(host["act8"])[rows], act[rows]):
                     failures.append(f"{lab}: act8")
                 checks = []

@@ -31,7 +31,7 @@ def test_run_fleet_and_compare_pass(tmp_path):
     rc, log = _run([ROOT / "oracle" / "run_reference.py", "--out", ref, "--layers", 3, "--iters", 4])
     assert rc == 0, log
     for n, (iters, extra, min_compared) in enumerate(((1, ["--debug"], 5), (4, [], 5),
-                                                      (1, ["--stop-after", "L1.w2_combine"], 12))):
+                                                      (1, ["--stop-after", "L1.combine"], 12))):
         out = tmp_path / f"fleet_{n}"
         rc, log = _run([HARNESS / "run_fleet.py", "--layers", 3, "--head", "--iters", iters, "--synthetic",
                         "--ref", ref, "--out", out, "--tile-linears", "--gemv-linears"] + extra)

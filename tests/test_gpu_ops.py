@@ -354,6 +354,49 @@ def test_moe_block(mk, B):
     assert_bits_equal(x_res, R.moe_combine(want_out8, topk_w, np32(x)), "combined x_res")
 
 
+@pytest.mark.parametrize("H,I,E,topk,nf", [(2048, 1408, 64, 6, 2), (64, 96, 8, 2, 2), (128, 256, 12, 3, 1),
+                                          (256, 1024, 8, 2, 1)])
+def test_moe_units_block(mk, B, H, I, E, topk, nf):
+    """The expert units: router -> the units of every slot (each task normalises x_res itself, runs
+    its share of the shared slots' units with their fixed experts, then its share of the routed
+    slots' units with the router's experts) -> the combine into x_res; out8, the
+    activations and x_res equal the oracle's staged arithmetic (w13 + SwiGLU, w2 row dots in the
+    row engine's order, moe_combine) bit for bit. The shapes cover 22 lanes in 8 parts (the model),
+    12 lanes in one part (classes of one and two lanes), 32 lanes in one part (four-lane classes)
+    and 32 lanes in four parts."""
+    from fleet.pack_weights import unit_parts
+    g = gen(43 + H)
+    ns = topk + nf
+    x = rnd_bf16(g, H)
+    w_norm = (1.0 + 0.5 * torch.randn(H, generator=g, device=DEV)).to(torch.bfloat16)
+    W_gate = rnd_bf16(g, E, H, std=0.05)
+    W13 = rnd_bf16(g, E + nf, 2 * I, H, std=0.02)
+    W2 = rnd_bf16(g, E + nf, H, I, std=0.02)
+    W2F = B.regrouped_w2(W2)
+    b = _router_bufs(E=E, NS=ns, H=H, L=1)
+    sums = torch.full((ns, unit_parts(I), 8, H), float("nan"), dtype=torch.float32, device=DEV)
+    act8 = torch.zeros(ns, I, dtype=torch.bfloat16, device=DEV)
+    out8 = torch.zeros(ns, H, dtype=torch.bfloat16, device=DEV)
+    x_res = x.clone()
+    ops = [B.moe_router_layer(mk, None, x_res, w_norm, W_gate, b["h"], b["topk_w"], b["routing"], b["mask"],
+                              b["logits"], b["route_log"], layer_index=0, topk=topk, n_experts=E, n_forced=nf,
+                              scaling=1.0, eps=1e-6),
+           B.moe_units_layer(mk, None, x_res, W13, W2F, sums, slot0=0, nslots=ns, inter=I, w_norm=w_norm,
+                             mask=b["mask"], act=act8, norm=True, fixed0=topk, static_experts=E),
+           B.moe_combine_layer(mk, None, sums, b["topk_w"], x_res, x_res, inter=I, out8=out8)]
+    run_ops(mk, ops)
+    dw = DeviceWeights({"W13": W13, "W2": W2})
+    h, logits, topk_w, routing, mask = R.moe_router_norm(np32(x), np32(w_norm), np32(W_gate), topk=topk,
+                                                         n_experts=E, forced=tuple(range(E, E + nf)))
+    assert np.array_equal(b["mask"].cpu().numpy()[:ns], mask[:ns])
+    want_act = np.stack([R.swiglu_act(R.linear(h, OracleModel.gate_up(dw.get_expert("W13", int(e)))), I)
+                         for e in mask[:ns]])
+    assert_bits_equal(act8, want_act, "act")
+    want_out8 = np.stack([R.linear(a, dw.get_expert("W2", int(e))) for a, e in zip(want_act, mask[:ns])])
+    assert_bits_equal(out8, want_out8, "out8")
+    assert_bits_equal(x_res, R.moe_combine(want_out8, topk_w, np32(x)), "combined x_res")
+
+
 def test_dense_mlp(mk, B):
     """Layer 0: norm2 + gate/up (+SwiGLU) over I 10,944, then the K-split down projection."""
     from fleet.pack_weights import REAL_DIMS as d
