@@ -29,7 +29,8 @@ P = dict(
     att=dict(QLNOPE=0, QPE=1, CKV=2, KPE=3, PARTIALS=4, SCORES=5),
     att_i=dict(NH=0, DC=1, DR=2, SMAX=3, SPLIT=4, HGROUP=5, NSPLITS=6, PROW=7, CPARTS=8),
     mrg=dict(PARTIALS=0, WUV=1, OUT=2), mrg_i=dict(NH=0, DV=1, DC=2, SPLIT=3, NSPLITS=4, PROW=5),
-    rt=dict(X=0, WNORM=1, WGATE=2, HOUT=3, LOGITS=4, TOPKW=5, ROUTING=6, MASK=7, ROUTELOG=8, BIAS=9),
+    rt=dict(X=0, WNORM=1, WGATE=2, HOUT=3, LOGITS=4, TOPKW=5, ROUTING=6, MASK=7, ROUTELOG=8, BIAS=9, LOGTAG=10,
+            MASKTAG=11),
     rt_i=dict(H=0, E=1, TOPK=2, NFORCED=3, LAYER=4, LOGSTRIDE=5, LOGROWS=6),
     gu=dict(X=0, WNORM=1, W=2, MASK=3, MID=4, ACT=5, HOUT=6),
     gu_i=dict(K=0, I=1, GROUPS=2, ESTRIDE=3, NEXP=4, EPRANK=5, EPWORLD=6, SLOT0=7),
@@ -37,7 +38,7 @@ P = dict(
     w2_i=dict(H=0, I=1, SLOTS=2, ESTRIDE=3, NEXP=4, TOPK=5, EPRANK=6, EPWORLD=7, LAYER=8),
     st=dict(W=0, OUT=1), st_i=dict(ROWS=0, K=1),
     cp=dict(SRC=0, DST=1), cp_i=dict(N=0),
-    mu=dict(X=0, WNORM=1, W13=2, W2F=3, MASK=4, SUMS=5, ACT=6, HOUT=7),
+    mu=dict(X=0, WNORM=1, W13=2, W2F=3, MASK=4, SUMS=5, ACT=6, HOUT=7, MASKTAG=8),
     mu_i=dict(H=0, I=1, SLOT0=2, NSLOTS=3, NS=4, NEXP=5, EXP0=6, FIXED0=7),
     mc=dict(SUMS=0, TOPKW=1, XRES=2, OUT8=3), mc_i=dict(H=0, I=1, NS=2),
 )

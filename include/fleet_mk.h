@@ -137,6 +137,11 @@ enum { /* MK_OP_MLA_MERGE_UV */ MK_P_MRG_PARTIALS = 0, MK_P_MRG_WUV = 1, MK_P_MR
 enum { /* MK_OP_ROUTER */ MK_P_RT_X = 0, MK_P_RT_WNORM = 1, MK_P_RT_WGATE = 2, MK_P_RT_HOUT = 3,
        MK_P_RT_LOGITS = 4, MK_P_RT_TOPKW = 5, MK_P_RT_ROUTING = 6, MK_P_RT_MASK = 7,
        MK_P_RT_ROUTELOG = 8, MK_P_RT_BIAS = 9,
+       MK_P_RT_LOGTAG = 10,  /* optional [E] 64-bit words: each logit with the iteration's tag in the high
+                                half. With it, task 0 routes once every task's tagged logits are there
+                                (no arrival counter) */
+       MK_P_RT_MASKTAG = 11, /* optional [TOPK + NFORCED] 64-bit words: the slots' experts with the
+                                iteration's tag in the high half (read by MOE_UNITS' MASKTAG) */
        MK_I_RT_H = 0, MK_I_RT_E = 1, MK_I_RT_TOPK = 2, MK_I_RT_NFORCED = 3, MK_I_RT_LAYER = 4,
        MK_I_RT_LOGSTRIDE = 5, MK_I_RT_LOGROWS = 6 };
 enum { /* MK_OP_GATEUP */ MK_P_GU_X = 0, MK_P_GU_WNORM = 1, MK_P_GU_W = 2, MK_P_GU_MASK = 3,
@@ -165,6 +170,9 @@ enum { /* MK_OP_W2_COMBINE */ MK_P_W2_ACT = 0, MK_P_W2_W = 1, MK_P_W2_MASK = 2, 
    (MK_F_NORM), so it needs no router output. */
 enum { /* MK_OP_MOE_UNITS */ MK_P_MU_X = 0, MK_P_MU_WNORM = 1, MK_P_MU_W13 = 2, MK_P_MU_W2F = 3, MK_P_MU_MASK = 4,
        MK_P_MU_SUMS = 5, MK_P_MU_ACT = 6 /* optional [NS][I] BF16 */, MK_P_MU_HOUT = 7 /* optional */,
+       MK_P_MU_MASKTAG = 8 /* optional: the router's tagged slot experts; the routed slots' weights stream
+                              as soon as their words carry the iteration's tag (no wait for the router's
+                              completion) */,
        MK_I_MU_H = 0, MK_I_MU_I = 1, MK_I_MU_SLOT0 = 2, MK_I_MU_NSLOTS = 3 /* slots of this operator */,
        MK_I_MU_NS = 4 /* all slots (SUMS, ACT) */, MK_I_MU_NEXP = 5, MK_I_MU_EXP0 = 6 /* MK_F_STATIC_IDS */,
        MK_I_MU_FIXED0 = 7 /* the first slot with a fixed expert (SLOT0 + NSLOTS: none) */ };

@@ -354,16 +354,19 @@ def test_moe_block(mk, B):
     assert_bits_equal(x_res, R.moe_combine(want_out8, topk_w, np32(x)), "combined x_res")
 
 
-@pytest.mark.parametrize("H,I,E,topk,nf", [(2048, 1408, 64, 6, 2), (64, 96, 8, 2, 2), (128, 256, 12, 3, 1),
-                                          (256, 1024, 8, 2, 1)])
-def test_moe_units_block(mk, B, H, I, E, topk, nf):
+@pytest.mark.parametrize("H,I,E,topk,nf,tags", [(2048, 1408, 64, 6, 2, True), (2048, 1408, 64, 6, 2, False),
+                                               (64, 96, 8, 2, 2, True), (128, 256, 12, 3, 1, False),
+                                               (256, 1024, 8, 2, 1, True)])
+def test_moe_units_block(mk, B, H, I, E, topk, nf, tags):
     """The expert units: router -> the units of every slot (each task normalises x_res itself, runs
     its share of the shared slots' units with their fixed experts, then its share of the routed
     slots' units with the router's experts) -> the combine into x_res; out8, the
     activations and x_res equal the oracle's staged arithmetic (w13 + SwiGLU, w2 row dots in the
     row engine's order, moe_combine) bit for bit. The shapes cover 22 lanes in 8 parts (the model),
     12 lanes in one part (classes of one and two lanes), 32 lanes in one part (four-lane classes)
-    and 32 lanes in four parts."""
+    and 32 lanes in four parts. tags: the router hands its logits to its task 0 and the slots'
+    experts to the units as tagged words (the decode graph's form), else through its arrival
+    counter and completion event."""
     from fleet.pack_weights import unit_parts
     g = gen(43 + H)
     ns = topk + nf
@@ -378,11 +381,16 @@ def test_moe_units_block(mk, B, H, I, E, topk, nf):
     act8 = torch.zeros(ns, I, dtype=torch.bfloat16, device=DEV)
     out8 = torch.zeros(ns, H, dtype=torch.bfloat16, device=DEV)
     x_res = x.clone()
+    tag = {}
+    if tags:
+        tag = dict(logit_tag=torch.zeros(E, dtype=torch.int64, device=DEV),
+                   mask_tag=torch.zeros(ns, dtype=torch.int64, device=DEV))
     ops = [B.moe_router_layer(mk, None, x_res, w_norm, W_gate, b["h"], b["topk_w"], b["routing"], b["mask"],
                               b["logits"], b["route_log"], layer_index=0, topk=topk, n_experts=E, n_forced=nf,
-                              scaling=1.0, eps=1e-6),
+                              scaling=1.0, eps=1e-6, **tag),
            B.moe_units_layer(mk, None, x_res, W13, W2F, sums, slot0=0, nslots=ns, inter=I, w_norm=w_norm,
-                             mask=b["mask"], act=act8, norm=True, fixed0=topk, static_experts=E),
+                             mask=b["mask"], act=act8, norm=True, fixed0=topk, static_experts=E,
+                             mask_tag=tag.get("mask_tag")),
            B.moe_combine_layer(mk, None, sums, b["topk_w"], x_res, x_res, inter=I, out8=out8)]
     run_ops(mk, ops)
     dw = DeviceWeights({"W13": W13, "W2": W2})
