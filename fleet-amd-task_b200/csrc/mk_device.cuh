@@ -38,11 +38,14 @@ __host__ __device__ inline int unit_q_vals(int q, int l8) {
   for (int k = 0; k < q; ++k) n += unit_lanes(k, l8);
   return 8 * n;
 }
-// gate/up rows per ring stage (a power of two dividing a lane's 16 rows)
-__host__ __device__ constexpr int unit_w13_rows(int64_t H) {
-  return STAGE_BYTES / (2 * H) >= 16 ? 16 : STAGE_BYTES / (2 * H) >= 8 ? 8 : STAGE_BYTES / (2 * H) >= 4 ? 4
-         : STAGE_BYTES / (2 * H) >= 2 ? 2 : 1;
+// gate/up rows of row_bytes each per ring stage (a power of two dividing a lane's 16 rows)
+__host__ __device__ constexpr int unit_w13_rows(int64_t row_bytes) {
+  return STAGE_BYTES / row_bytes >= 16 ? 16 : STAGE_BYTES / row_bytes >= 8 ? 8 : STAGE_BYTES / row_bytes >= 4 ? 4
+         : STAGE_BYTES / row_bytes >= 2 ? 2 : 1;
 }
+// regrouped down-projection rows of row_bytes each per ring stage: an even count, so a stage's
+// bytes and its source offset stay multiples of 16 for FP8 rows of 8 nl bytes
+__host__ __device__ constexpr int unit_w2_rows(int row_bytes) { return (STAGE_BYTES / row_bytes) & ~1; }
 // the down projection's slot weights and slot outputs follow its activations (16-byte aligned)
 __host__ __device__ constexpr int w2_aux_off(int ns, int inter) { return (ns * inter * 2 + 15) / 16 * 16; }
 __host__ __device__ constexpr int w2_aux_bytes(int ns, int rows) { return (MAX_ROUTED + ns * rows) * 4; }
@@ -121,6 +124,8 @@ struct __align__(128) Smem {
   int32_t wbest_i[NUM_CONSUMER_WARPS];
   int32_t bcast[8];
   uint32_t cta_abort;
+  int32_t stage_aux[NSTAGES];   // a word the producer attaches to a stage (written before the stage's
+                                // arrive, so the consumer that acquired the stage sees it)
   uint64_t tr[4];           // trace stamps of the running task (TR_*), thread 0
   KernelParams kp;          // the launch parameters
   __align__(16) OpDev od_buf[2];     // the running task's operator and the next one's (copied ahead)

@@ -19,7 +19,7 @@ sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 from fleet import graph_plan as G  # noqa: E402
 from fleet.pack_weights import Dims, REAL_DIMS  # noqa: E402
 
-TORCH_DTYPES = {"bf16": "bfloat16", "f32": "float32", "i32": "int32", "i64": "int64"}
+TORCH_DTYPES = {"bf16": "bfloat16", "f32": "float32", "i32": "int32", "i64": "int64", "u8": "uint8"}
 
 
 # ----------------------------------------------------------------------------
@@ -126,20 +126,25 @@ def moe_w2_combine_layer(mk, t, input, weight, mask, topk_w, residual, output, o
 
 
 def moe_units_layer(mk, t, input, w13, w2f, sums, slot0, nslots, inter, w_norm=None, mask=None, act=None,
-                    h_out=None, norm=False, fixed0=None, static_experts=None, mask_tag=None, eps=G.RMS_EPS):
+                    h_out=None, norm=False, fixed0=None, static_experts=None, mask_tag=None, scale13=None,
+                    eps=G.RMS_EPS):
     """Expert units of slots [slot0, slot0 + nslots): gate/up + SwiGLU of each unit's intermediates
     and the down projection's butterfly subtree sums into `sums` [NS, parts, 8, H]. w13 [E, 2I, H]
     (gate/up interleaved), w2f the down projection regrouped by unit (pack_weights.regroup_w2).
     Slots from fixed0 on use experts static_experts, static_experts + 1, ... (the shared experts,
     no router); the slots before fixed0 take theirs from `mask` once the router is done. Every
     task runs a share of the fixed slots' units, then a share of the routed slots'. mask_tag: the
-    router's tagged slot experts (the routed weights stream as soon as those words are in)."""
+    router's tagged slot experts (the routed weights stream as soon as those words are in).
+    scale13 [E, 2] FP32: FP8 experts (fleet_mk.h MK_F_FP8), w13 and w2f then hold E4M3 codes
+    (pack_weights.fp8_experts) and scale13 the gate and up scales."""
     E, two_i, H = w13.shape
     assert two_i == 2 * inter and w2f.shape == (E, H * inter), (tuple(w13.shape), tuple(w2f.shape))
     ns = sums.shape[0]
     fixed0 = slot0 + nslots if fixed0 is None else fixed0
     assert slot0 <= fixed0 <= slot0 + nslots and (fixed0 == slot0 + nslots or static_experts is not None)
-    flags = (mk.F_NORM if norm else 0) | (mk.F_EXPERT if fixed0 > slot0 else 0)
+    flags = (mk.F_NORM if norm else 0) | (mk.F_EXPERT if fixed0 > slot0 else 0) | (mk.F_FP8 if scale13 is not None
+                                                                                     else 0)
+    assert scale13 is None or tuple(scale13.shape) == (E, 2), tuple(scale13.shape)
     ips = {0: H, 1: inter, 2: slot0, 3: nslots, 4: ns, 5: E, 7: fixed0}
     if fixed0 < slot0 + nslots:
         flags |= mk.F_STATIC_IDS
@@ -147,17 +152,21 @@ def moe_units_layer(mk, t, input, w13, w2f, sums, slot0, nslots, inter, w_norm=N
     u = mk.P["mu"]
     return mk.make_op(mk.OP_MOE_UNITS, flags, {u["X"]: input, u["WNORM"]: w_norm, u["W13"]: w13, u["W2F"]: w2f,
                                                u["MASK"]: mask, u["SUMS"]: sums, u["ACT"]: act, u["HOUT"]: h_out,
-                                               u["MASKTAG"]: mask_tag},
+                                               u["MASKTAG"]: mask_tag, u["SCALE13"]: scale13},
                       ips, {0: eps})
 
 
-def moe_combine_layer(mk, t, sums, topk_w, residual, output, inter, out8=None):
+def moe_combine_layer(mk, t, sums, topk_w, residual, output, inter, out8=None, mask=None, scale2=None):
     """out8 = bf16(down projection) per slot from the units' subtree sums, then
-    x_res = bf16(x_res + sum_s f32(out8_s w_s)) (numpy_ref.moe_combine), in place."""
+    x_res = bf16(x_res + sum_s f32(out8_s w_s)) (numpy_ref.moe_combine), in place. scale2 [E] FP32:
+    FP8 experts, each slot's down projection times its expert's (mask[s]) scale before the rounding."""
     assert residual.data_ptr() == output.data_ptr(), "the combine adds into x_res in place"
+    assert scale2 is None or mask is not None, "FP8 down scales need the slots' experts"
     ns, H = sums.shape[0], sums.shape[-1]
     c = mk.P["mc"]
-    return mk.make_op(mk.OP_MOE_COMBINE, 0, {c["SUMS"]: sums, c["TOPKW"]: topk_w, c["XRES"]: output, c["OUT8"]: out8},
+    return mk.make_op(mk.OP_MOE_COMBINE, mk.F_FP8 if scale2 is not None else 0,
+                      {c["SUMS"]: sums, c["TOPKW"]: topk_w, c["XRES"]: output, c["OUT8"]: out8,
+                       c["MASK"]: mask if scale2 is not None else None, c["SCALE2"]: scale2},
                       {0: H, 1: inter, 2: ns})
 
 
@@ -228,6 +237,23 @@ def regrouped_w2(w2):
     return f
 
 
+_FP8 = {}
+
+
+def fp8_experts(w13, w2):
+    """pack_weights.fp8_experts(w13, w2) as a dict (W13q, s13, W2Fq, s2), computed once per W13
+    tensor and dropped with it."""
+    import weakref
+    from fleet.pack_weights import fp8_experts as quantize
+    hit = _FP8.get(id(w13))
+    if hit is not None and hit[0]() is w13:
+        return hit[1]
+    f = dict(zip(("W13q", "s13", "W2Fq", "s2"), quantize(w13, w2)))
+    _FP8[id(w13)] = (weakref.ref(w13), f)
+    weakref.finalize(w13, _FP8.pop, id(w13), None)
+    return f
+
+
 def make_tensors(plan, packed, capture, meta, torch, workspaces=None, device="cuda", align=0):
     """name -> torch tensor for every plan tensor: inputs attached (shape-checked), the rest zeroed."""
     host = {}
@@ -243,6 +269,9 @@ def make_tensors(plan, packed, capture, meta, torch, workspaces=None, device="cu
                 src = capture[t.source[8:]]
             elif t.source.startswith("regroup_w2:"):   # the down projection regrouped by expert unit
                 src = regrouped_w2(packed[t.source[11:]])
+            elif t.source.startswith("fp8:"):          # fp8:<part>:<layer>, the layer's FP8 experts
+                part, layer = t.source[4:].split(":")
+                src = fp8_experts(packed[f"W13_{layer}"], packed[f"W2_{layer}"])[part]
             else:
                 src = packed[t.source]
             assert tuple(src.shape) == t.shape, (t.name, tuple(src.shape), t.shape)
@@ -481,7 +510,7 @@ class FakeMk:
     """Records operators instead of calling the library (the reference's FakeMPK role)."""
     OP_EMBED, OP_GEMV, OP_MLA_PREP, OP_MLA_ATTEND, OP_MLA_MERGE_UV, OP_ROUTER, OP_GATEUP, OP_W2_COMBINE, OP_STREAM, \
         OP_COPY, OP_MOE_UNITS, OP_MOE_COMBINE = range(1, 13)
-    F_NORM, F_RESIDUAL, F_ARGMAX, F_EXPERT, F_STATIC_IDS, F_EP, F_TC = 1, 2, 4, 8, 16, 32, 64
+    F_NORM, F_RESIDUAL, F_ARGMAX, F_EXPERT, F_STATIC_IDS, F_EP, F_TC, F_FP8 = 1, 2, 4, 8, 16, 32, 64, 128
 
     def __init__(self):
         from fleet.mk import P

@@ -269,13 +269,16 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
     tc_parts: its latent-column parts per split (one task each).
     moe: "units" (the default on one GPU): the experts as units (slot, down-projection part, lane
     class) that each run gate/up, SwiGLU and their share of the down projection, every task the
-    shared slots' units first and the routed slots' once the router is done, then a combine; "staged" (the default, and the only form,
+    shared slots' units first and the routed slots' once the router is done, then a combine;
+    "units_fp8": the same with weight-only FP8 experts (E4M3 codes, one scale per gate, up and
+    down tensor of each expert, fleet_mk.h MK_F_FP8); "staged" (the default, and the only form,
     with ep): gate/up of the shared and of the routed slots, then the down projection and combine
     over all slots."""
     if moe is None:
         moe = "units" if ep is None else "staged"
-    if moe not in ("units", "staged") or (moe == "units" and ep is not None):
-        raise ValueError(f"moe={moe!r}: 'units' (one GPU) or 'staged'")
+    if moe not in ("units", "units_fp8", "staged") or (moe != "staged" and ep is not None):
+        raise ValueError(f"moe={moe!r}: 'units' or 'units_fp8' (one GPU), or 'staged'")
+    units = moe in ("units", "units_fp8")
     variants = mi300_variants(tile_linears, attend_tasks, fuse_norm2, fuse_silu, fuse_norm1, prefetch, gemv_linears,
                               linear_grid, head_grid, gemv_w13, merge_tasks, merge_halves, router_tasks,
                               merge_oproj, argmax_slices)
@@ -320,7 +323,7 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
         p.t("mid", (d.N_SLOTS, 2 * d.I_MOE))
         p.t("act8", (d.N_SLOTS, d.I_MOE))
         p.t("out8", (d.N_SLOTS, d.H))
-        if moe == "units":
+        if units:
             p.t("moe_sums", (d.N_SLOTS, unit_parts(d.I_MOE), 8, d.H), "f32")
             p.t("logit_tag", (d.L - 1, d.E), "i64")          # per MoE layer: tagged-word hand-offs
             p.t("mask_tag", (d.L - 1, d.N_SLOTS), "i64")
@@ -362,8 +365,14 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
                  residual_add=True)
         else:
             p.t(f"W_gate_{l}", (d.E, d.H), kind="input", source=f"W_gate_{l}")
-            p.t(f"W13_{l}", (d.E_TOTAL, 2 * d.I_MOE, d.H), kind="input", source=f"W13_{l}")
-            if moe == "units":
+            if moe != "units_fp8":
+                p.t(f"W13_{l}", (d.E_TOTAL, 2 * d.I_MOE, d.H), kind="input", source=f"W13_{l}")
+            if moe == "units_fp8":   # the experts' E4M3 codes and scales, quantised from W13 / W2
+                p.t(f"W13Q_{l}", (d.E_TOTAL, 2 * d.I_MOE, d.H), "u8", "input", f"fp8:W13q:{l}")
+                p.t(f"S13_{l}", (d.E_TOTAL, 2), "f32", "input", f"fp8:s13:{l}")
+                p.t(f"W2FQ_{l}", (d.E_TOTAL, d.H * d.I_MOE), "u8", "input", f"fp8:W2Fq:{l}")
+                p.t(f"S2_{l}", (d.E_TOTAL,), "f32", "input", f"fp8:s2:{l}")
+            elif moe == "units":
                 p.t(f"W2F_{l}", (d.E_TOTAL, d.H * d.I_MOE), kind="input", source=f"regroup_w2:W2_{l}")
             else:
                 p.t(f"W2_{l}", (d.E_TOTAL, d.H, d.I_MOE), kind="input", source=f"W2_{l}")
@@ -371,23 +380,26 @@ def build_plan(dims: Dims = REAL_DIMS, s_max: int = 1056, layers: int = 27, head
             if logit_bias:
                 p.t(f"router_bias_{l}", (d.E,), "f32", kind="input", source=f"capture:router_bias_{l}")
                 bias = dict(bias=f"router_bias_{l}")
-            tags = dict(logit_tag=Rows("logit_tag", l - 1), mask_tag=Rows("mask_tag", l - 1)) if moe == "units" else {}
+            tags = dict(logit_tag=Rows("logit_tag", l - 1), mask_tag=Rows("mask_tag", l - 1)) if units else {}
             p.op("moe_router_layer", f"L{l}.router", input="x_res", w_norm=f"w_norm2_{l}", w_gate=f"W_gate_{l}",
                  h="h", topk_w="topk_w", routing="routing", mask="mask", logits="logits_router",
                  route_log="route_log", layer_index=l - 1, topk=d.TOPK, n_experts=d.E, n_forced=d.N_SHARED,
                  scaling=ROUTED_SCALING, eps=RMS_EPS, **bias, **tags)
-            if moe == "units":
+            if units:
                 # the expert units (fleet_mk.h MK_OP_MOE_UNITS), on the CTAs the router leaves free:
                 # every task normalises x_res itself, runs its share of the shared slots' units at
                 # once and its share of the routed slots' units when the router's expert ids are out;
                 # the combine adds all slots
                 p.op("moe_units_layer", f"L{l}.experts", deps=(f"L{l}.o_proj",), beside=(f"L{l}.router",),
                      input="x_res",
-                     w_norm=f"w_norm2_{l}", w13=f"W13_{l}", w2f=f"W2F_{l}", mask="mask", sums="moe_sums",
+                     w_norm=f"w_norm2_{l}", mask="mask", sums="moe_sums",
                      act="act8", slot0=0, nslots=d.N_SLOTS, fixed0=d.TOPK, static_experts=d.E, norm=True,
-                     mask_tag=Rows("mask_tag", l - 1), inter=d.I_MOE, eps=RMS_EPS)
+                     mask_tag=Rows("mask_tag", l - 1), inter=d.I_MOE, eps=RMS_EPS,
+                     **(dict(w13=f"W13Q_{l}", w2f=f"W2FQ_{l}", scale13=f"S13_{l}") if moe == "units_fp8"
+                        else dict(w13=f"W13_{l}", w2f=f"W2F_{l}")))
                 p.op("moe_combine_layer", f"L{l}.combine", deps=(f"L{l}.experts", f"L{l}.router"),
-                     sums="moe_sums", topk_w="topk_w", residual="x_res", output="x_res", out8="out8", inter=d.I_MOE)
+                     sums="moe_sums", topk_w="topk_w", residual="x_res", output="x_res", out8="out8", inter=d.I_MOE,
+                     **(dict(mask="mask", scale2=f"S2_{l}") if moe == "units_fp8" else {}))
                 if debug:
                     p.op("copy_layer", f"L{l}.snapshot", note="debug only: per-layer residual snapshot",
                          input="x_res", output=f"dbg_x_res_{l}")
@@ -443,7 +455,7 @@ def summary(p: Plan) -> dict:
             n = 1
             for s in t.shape:
                 n *= s
-            ib += n * {"bf16": 2, "f32": 4, "i32": 4, "i64": 8}[t.dtype]
+            ib += n * {"bf16": 2, "f32": 4, "i32": 4, "i64": 8, "u8": 1}[t.dtype]
     return {"ops": p.n_ops, "tasks": p.n_tasks, "tensors_new": sum(t.kind == "new" for t in p.tensors.values()),
             "tensors_input": sum(t.kind == "input" for t in p.tensors.values()), "input_bytes": ib,
             "n_splits": p.n_splits}

@@ -224,6 +224,32 @@ def regroup_w2(W2):
     return torch.cat(pieces, dim=2).reshape(E, H * I).contiguous()
 
 
+E4M3_MAX = 448.0
+
+
+def quantize_e4m3(w, groups=1):
+    """Weight-only FP8 (the reference's D26): w [E, R, K] BF16 -> (q [E, R, K] uint8 E4M3 codes,
+    scale [E, groups] float32). Rows r with r mod groups = g form one tensor with one scale,
+    amax / 448 (1 for an all-zero tensor); q = e4m3(w / scale), the quotient in FP32, rounded to
+    the nearest E4M3 value (ties to even), |w / scale| <= 448 by construction. groups = 2 for the
+    interleaved gate/up rows of W13 (gate and up are separate tensors in a checkpoint)."""
+    E, R, K = w.shape
+    assert R % groups == 0
+    wf = w.float().reshape(E, R // groups, groups, K)
+    amax = wf.abs().amax(dim=(1, 3))
+    scale = torch.where(amax > 0, amax / E4M3_MAX, torch.ones_like(amax))
+    q = (wf / scale[:, None, :, None]).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn)
+    return q.view(torch.uint8).reshape(E, R, K).contiguous(), scale.contiguous()
+
+
+def fp8_experts(W13, W2):
+    """The expert units' FP8 tensors of one layer: (W13q [E, 2I, H] uint8, s13 [E, 2], W2Fq
+    [E, H * I] uint8 regrouped as regroup_w2 orders it, s2 [E])."""
+    W13q, s13 = quantize_e4m3(W13, 2)
+    W2q, s2 = quantize_e4m3(W2, 1)
+    return W13q, s13, regroup_w2(W2q), s2.reshape(-1).contiguous()
+
+
 def pack_attention(d: Dims, get):
     """The attention and norm tensors of one layer; get(suffix) -> the layer's tensor."""
     w_uk, w_uv = split_uk_uv(d, get("self_attn.kv_b_proj.weight"))
@@ -288,24 +314,26 @@ def packed_bytes(d: Dims, bf16=2):
     return 2 * d.V * d.H * bf16 + d.H * bf16 + sum(layer_bytes(d, l, bf16) for l in range(d.L))
 
 
-def active_bytes_per_token(d: Dims, ctx=1024, layers=None, head=True, bf16=2):
+def active_bytes_per_token(d: Dims, ctx=1024, layers=None, head=True, bf16=2, expert_bytes=None):
     """Algorithmic HBM bytes of one decode token, counted as the reference's roofline counts
     them (docs/deepseek-v2-lite/sources/roofline.py; 07-roofline.md:30-55): every attention and
     dense-MLP weight matrix, the router, the shared and TOPK routed experts of each MoE layer,
     lm_head, and `ctx` latent-cache rows per layer. Norm weights and the embedding row (under
-    0.01%) are not counted. At REAL_DIMS, ctx 1024: 4,934,467,584 B."""
+    0.01%) are not counted. At REAL_DIMS, ctx 1024: 4,934,467,584 B. expert_bytes: bytes per
+    expert weight (1 for the FP8 experts, whose scales are 12 bytes an expert; default bf16)."""
     layers = d.L if layers is None else layers
+    eb = bf16 if expert_bytes is None else expert_bytes
     attn = d.Q_OUT * d.H + d.KVA_OUT * d.H + d.KVB_OUT * d.D_C + d.H * d.NH * d.D_V
     total = 0
     for l in range(layers):
-        total += attn + ctx * (d.D_C + d.D_R)
+        total += (attn + ctx * (d.D_C + d.D_R)) * bf16
         if l == 0:
-            total += 3 * d.I_DENSE * d.H
+            total += 3 * d.I_DENSE * d.H * bf16
         else:
-            total += d.E * d.H + d.N_SLOTS * 3 * d.I_MOE * d.H
+            total += d.E * d.H * bf16 + d.N_SLOTS * 3 * d.I_MOE * d.H * eb
     if head:
-        total += d.V * d.H
-    return total * bf16
+        total += d.V * d.H * bf16
+    return total
 
 
 def routed_bytes_per_token(d: Dims, layers=None, bf16=2):

@@ -3,7 +3,7 @@
 
     python harness/run_fleet.py --layers N [--head] [--iters K] [--debug] [--debug-scores]
         [--stop-after L1.o_proj] (--model-dir SNAPSHOT | --synthetic) [--ref REF_DIR] [--out DIR]
-        [--split N] [--attend-tc] [--moe units|staged] [--event-timing] [--align-alloc BYTES] [--workspaces-first]
+        [--split N] [--attend-tc] [--moe units|units_fp8|staged] [--event-timing] [--align-alloc BYTES] [--workspaces-first]
         [the reference's variant switches: --tile-linears ... --merge-oproj, recorded]
 
 The driver of the reference (harness/run_fleet.py:505-616), against this package: positions follow
@@ -138,7 +138,8 @@ def build_parser():
     ap.add_argument("--out", required=True)
     ap.add_argument("--split", type=int, default=None, help="cache rows per attention split")
     ap.add_argument("--attend-tc", action="store_true", help="the MLA attention on the tensor cores")
-    ap.add_argument("--moe", default=None, choices=["units", "staged"], help="the experts' form (default: units)")
+    ap.add_argument("--moe", default=None, choices=["units", "units_fp8", "staged"],
+                    help="the experts' form (default: units; units_fp8: weight-only FP8 experts)")
     ap.add_argument("--event-timing", action="store_true", help="per-task %%globaltimer stamps (event_timing.json)")
     ap.add_argument("--align-alloc", type=int, default=0, help="re-base weights, capture and workspaces on BYTES")
     ap.add_argument("--workspaces-first", action="store_true", help="allocate the workspaces before the weights")

@@ -99,6 +99,13 @@ enum MkOpType {
                                     tensor cores' order, so its partials match the specified-order
                                     form within rounding, not bit for bit */
 
+#define MK_F_FP8 (1 << 7)        /* MOE_UNITS / MOE_COMBINE: weight-only FP8 experts (the reference's D26):
+                                    W13 and W2F hold E4M3 codes (one byte), one scale per tensor (gate,
+                                    up and down of each expert); the activations are rounded to FP16
+                                    for the products, which are exact in FP32 (4 and 11 significant
+                                    bits), the sums run in the BF16 form's order, and each row's total
+                                    is multiplied by its tensor's scale before the BF16 rounding */
+
 #define MK_MAX_PTRS 16
 #define MK_MAX_IPARAMS 16
 
@@ -175,11 +182,13 @@ enum { /* MK_OP_MOE_UNITS */ MK_P_MU_X = 0, MK_P_MU_WNORM = 1, MK_P_MU_W13 = 2, 
                               completion) */,
        MK_I_MU_H = 0, MK_I_MU_I = 1, MK_I_MU_SLOT0 = 2, MK_I_MU_NSLOTS = 3 /* slots of this operator */,
        MK_I_MU_NS = 4 /* all slots (SUMS, ACT) */, MK_I_MU_NEXP = 5, MK_I_MU_EXP0 = 6 /* MK_F_STATIC_IDS */,
-       MK_I_MU_FIXED0 = 7 /* the first slot with a fixed expert (SLOT0 + NSLOTS: none) */ };
+       MK_I_MU_FIXED0 = 7 /* the first slot with a fixed expert (SLOT0 + NSLOTS: none) */,
+       MK_P_MU_SCALE13 = 9 /* MK_F_FP8: [experts][2] FP32, the gate and up scales */ };
 /* MK_OP_MOE_COMBINE: per row r and slot s, the down projection's part sums
    ((S_0 + S_4) + (S_2 + S_6)) + ((S_1 + S_5) + (S_3 + S_7)) added in part order, rounded to BF16
    (out8), then x_res = bf16(x_res + sum_s f32(out8_s w_s)) in slot order. */
 enum { /* MK_OP_MOE_COMBINE */ MK_P_MC_SUMS = 0, MK_P_MC_TOPKW = 1, MK_P_MC_XRES = 2, MK_P_MC_OUT8 = 3 /* optional */,
+       MK_P_MC_MASK = 4, MK_P_MC_SCALE2 = 5 /* MK_F_FP8: the slots' experts and [experts] FP32 down scales */,
        MK_I_MC_H = 0, MK_I_MC_I = 1, MK_I_MC_NS = 2 };
 /* Expert parallelism: where each rank's exchange words are, as this rank maps them (peer pointers
    opened with mk_ep_ipc_open). xch[r] is rank r's [2][n_layers][n_slots][hidden / 2] array of

@@ -22,7 +22,7 @@ from oracle.detmath import F32
 
 class OracleModel:
     def __init__(self, dims, get, get_expert=None, *, softmax_scale, split=32, eps=1e-6,
-                 layers=None, head=True, logit_bias=None):
+                 layers=None, head=True, logit_bias=None, fp8=None):
         self.d = dims
         self.get = get
         self.get_expert = get_expert or (lambda name, e: get(name)[e])
@@ -32,6 +32,9 @@ class OracleModel:
         self.layers = dims.L if layers is None else layers
         self.head = head
         self.logit_bias = logit_bias          # {layer: [E] FP32} injected routing (config 3)
+        # FP8 experts: fp8(l, e) -> (W13q [2I, H], s13 [2], W2q [H, I], s2), E4M3 codes (uint8) and
+        # the expert's gate, up and down scales; the experts then run numpy_ref.linear_fp8
+        self.fp8 = fp8
 
     def W_uk(self, l):
         return np.ascontiguousarray(self.get(f"W_ukT_{l}").transpose(0, 2, 1))
@@ -78,6 +81,12 @@ class OracleModel:
         out8 = np.full((n_slots, d.H), np.nan, F32)
         for s in range(int(mask[-1])):
             e = int(mask[s])
+            if self.fp8 is not None:
+                w13q, s13, w2q, s2 = self.fp8(l, e)
+                mid[s] = np.concatenate([R.linear_fp8(h, w13q[0::2], s13[0]), R.linear_fp8(h, w13q[1::2], s13[1])])
+                act = R.swiglu_act(mid[s], d.I_MOE)
+                out8[s] = R.linear_fp8(act, w2q, s2)
+                continue
             mid[s] = R.linear(h, self.gate_up(self.get_expert(f"W13_{l}", e)))
             act = R.swiglu_act(mid[s], d.I_MOE)
             out8[s] = R.linear(act, self.get_expert(f"W2_{l}", e))

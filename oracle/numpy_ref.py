@@ -25,7 +25,7 @@ __all__ = ["bf16", "rmsnorm", "rope", "mla_prep", "mla_attend", "merge_partials"
            "attention_decompressed",
            "moe_router", "moe_router_norm", "moe_w13", "moe_w2", "silu", "linear", "linear_norm",
            "linear_residual", "moe_combine", "dense_mlp", "embed", "lm_head_argmax",
-           "partials_row", "softmax_det"]
+           "partials_row", "softmax_det", "e4m3", "f16", "linear_fp8", "moe_experts_fp8"]
 
 
 def partials_row(d_c):
@@ -336,3 +336,66 @@ def lm_head_argmax(x_res, w_final_norm, W_lm, eps=1e-6):
     h = rmsnorm(x_res, w_final_norm, eps)
     logits = linear(h, W_lm)
     return h, logits, int(np.argmax(logits))
+
+
+# ---------------------------------------------------------------------------------------------
+# FP8 weight-only experts (the reference's D26 plan, docs/acceleration/01-precision.md:125-165:
+# E4M3 weights with a per-tensor scale, BF16 activations, FP32 accumulation; no FP8 kernel of the
+# reference exists, so the arithmetic below is this build's specified form)
+
+
+def e4m3_table():
+    """float32 value of every E4M3 byte (OCP FP8 E4M3FN: bias 7, subnormals m * 2^-9, 0x7F / 0xFF
+    NaN, no infinity), from the format's definition."""
+    t = np.empty(256, F32)
+    for b in range(256):
+        s, e, m = b >> 7, (b >> 3) & 15, b & 7
+        if e == 15 and m == 7:
+            v = np.nan
+        elif e == 0:
+            v = m * 2.0 ** -9
+        else:
+            v = (1.0 + m / 8.0) * 2.0 ** (e - 7)
+        t[b] = -v if s else v
+    return t
+
+
+_E4M3 = None
+
+
+def e4m3(q):
+    """uint8 E4M3 codes -> float32 values (exact)."""
+    global _E4M3
+    if _E4M3 is None:
+        _E4M3 = e4m3_table()
+    return _E4M3[np.asarray(q, np.uint8)]
+
+
+def f16(x):
+    """float32 values rounded to FP16 (nearest even) and back: the FP8 path's activation operand."""
+    return np.asarray(x, F32).astype(np.float16).astype(F32)
+
+
+def linear_fp8(x, Wq, scale):
+    """bf16(scale * (E4M3 rows . fp16(x))): each product of an E4M3 value (4 significant bits) and an
+    FP16 value (11) is exact in FP32, the sum runs in the row-dot order, one FP32 multiply by the
+    tensor's scale, one BF16 rounding."""
+    return bf16((F32(scale) * dot_rows(e4m3(Wq), f16(x))).astype(F32))
+
+
+def moe_experts_fp8(h, W13q, s13, W2q, s2, mask, n_slots=8):
+    """The experts with E4M3 weights: per slot s (expert e = mask[s]) gate = linear_fp8(h, rows 2i of
+    W13q[e], s13[e, 0]), up likewise with rows 2i + 1 and s13[e, 1], act = bf16(silu(gate) up),
+    out8[s] = linear_fp8(act, W2q[e], s2[e]). W13q [E, 2I, H] (gate and up interleaved), W2q
+    [E, H, I], uint8. Returns (act [n_slots, I], out8 [n_slots, H])."""
+    W13q = np.asarray(W13q)
+    I = W13q.shape[1] // 2
+    act = np.full((n_slots, I), np.nan, F32)
+    out8 = np.full((n_slots, np.shape(W2q)[1]), np.nan, F32)
+    for s in range(int(mask[-1])):
+        e = int(mask[s])
+        g = linear_fp8(h, W13q[e][0::2], s13[e][0])
+        u = linear_fp8(h, W13q[e][1::2], s13[e][1])
+        act[s] = swiglu_act(np.concatenate([g, u]), I)
+        out8[s] = linear_fp8(act[s], W2q[e], s2[e])
+    return act, out8

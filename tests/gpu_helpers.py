@@ -57,6 +57,24 @@ class DeviceWeights:
         return self.cache[key]
 
 
+class DeviceFP8:
+    """The oracle's FP8 expert accessor, fp8(l, e): each layer's W13 / W2 quantised on the device as
+    the FP8 graph quantises them (pack_weights.quantize_e4m3), one expert's codes and scales copied
+    to the host on use."""
+
+    def __init__(self, packed):
+        self.packed = packed
+        self.layers = {}
+
+    def __call__(self, l, e):
+        from fleet.pack_weights import quantize_e4m3
+        if l not in self.layers:
+            self.layers[l] = quantize_e4m3(self.packed[f"W13_{l}"], 2) + quantize_e4m3(self.packed[f"W2_{l}"], 1)
+        W13q, s13, W2q, s2 = self.layers[l]
+        return (W13q[e].cpu().numpy(), s13[e].cpu().numpy(), W2q[e].cpu().numpy(),
+                np.float32(s2[e, 0].item()))
+
+
 def u16(t):
     """A BF16 device tensor as its uint16 bit patterns on the host."""
     return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)

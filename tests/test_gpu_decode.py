@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_helpers import DeviceWeights, assert_bits_equal, np32
+from gpu_helpers import DeviceFP8, DeviceWeights, assert_bits_equal, np32
 from oracle.detmath import from_bf16_bits
 from oracle.model import OracleModel
 
@@ -18,7 +18,7 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 
 
-def build_model(layers, iters, n_past=1023, seed=0, random_norms=True, dims=None, split=None):
+def build_model(layers, iters, n_past=1023, seed=0, random_norms=True, dims=None, split=None, moe=None):
     from fleet import build_graph as B
     from fleet import graph_plan as G
     from fleet.capture import make_capture
@@ -31,6 +31,8 @@ def build_model(layers, iters, n_past=1023, seed=0, random_norms=True, dims=None
     meta = B.make_meta(torch, s_max, prompt.tolist(), n_past + 1, device=DEV)
     cache0 = {k: np32(v) for k, v in capture.items() if k.startswith(("c_kv_", "k_pe_"))}
     kw = {} if split is None else dict(split=split)
+    if moe is not None:
+        kw["moe"] = moe
     mpk, host, plan = B.build(packed, capture, meta, dims=d, s_max=s_max, layers=layers, head=True, **kw)
     return d, packed, capture, meta, cache0, mpk, host, plan, n_past
 
@@ -39,7 +41,7 @@ def oracle_run(d, packed, capture, meta, cache0, plan, layers, iters, pos0):
     from fleet.capture import softmax_scale
     dw = DeviceWeights(packed)
     m = OracleModel(d, dw.get, dw.get_expert, softmax_scale=softmax_scale(d.D_N, d.D_R), split=plan.split,
-                    layers=layers)
+                    layers=layers, fp8=DeviceFP8(packed) if plan.moe == "units_fp8" else None)
     tokens = meta["tokens"][0].cpu().numpy().copy()
     cache = {k: v.copy() for k, v in cache0.items()}
     cos, sin = np32(capture["cos"]), np32(capture["sin"])
@@ -75,6 +77,33 @@ def test_decode_one_launch_matches_oracle(layers, iters):
     L = layers - 1
     assert np.array_equal(host["mask"].cpu().numpy(), rec[f"L{L}.mask"])
     assert_bits_equal(host["out8"], rec[f"L{L}.out8"], "out8")
+
+
+def test_decode_fp8_experts_matches_oracle():
+    """The FP8-expert graph (moe="units_fp8": E4M3 expert weights quantised per tensor from the
+    BF16 checkpoint, fleet_mk.h MK_F_FP8): a dense layer, two MoE layers and the head, three greedy
+    iterations in one launch; ids, route log, cache rows, logits and out8 equal the oracle running
+    the same FP8 experts bit for bit."""
+    layers = 3
+    d, packed, capture, meta, cache0, mpk, host, plan, pos0 = build_model(layers, 3, seed=3, moe="units_fp8")
+    assert plan.moe == "units_fp8" and "W13_1" not in host and host["W13Q_1"].dtype == torch.uint8
+    mpk.compile()
+    meta["step"].fill_(pos0 - 1)
+    mpk()
+    assert mpk.status()["error"] == 0
+    n_run = plan.s_max - 2 - (pos0 - 1)
+    ids = meta["tokens"][0, pos0 + 1: pos0 + 1 + n_run].tolist()
+    want_ids, routes, rec, cache = oracle_run(d, packed, capture, meta, cache0, plan, layers, n_run, pos0)
+    assert ids == want_ids
+    rl = host["route_log"].cpu().numpy()
+    for i in range(n_run):
+        for l in range(1, layers):
+            assert rl[i, l - 1, :d.TOPK].tolist() == routes[i][l - 1], (i, l)
+    for l in range(layers):
+        got = host[f"c_kv_{l}"][pos0:pos0 + n_run].float().cpu().numpy()
+        assert np.array_equal(got, cache[f"c_kv_{l}"][pos0:pos0 + n_run]), l
+    assert_bits_equal(host["logits"][0], rec["head.logits"], "logits")
+    assert_bits_equal(host["out8"], rec[f"L{layers - 1}.out8"], "out8")
 
 
 def test_decode_launch_per_token_equals_one_launch():

@@ -405,6 +405,48 @@ def test_moe_units_block(mk, B, H, I, E, topk, nf, tags):
     assert_bits_equal(x_res, R.moe_combine(want_out8, topk_w, np32(x)), "combined x_res")
 
 
+@pytest.mark.parametrize("H,I,E,topk,nf", [(2048, 1408, 64, 6, 2), (64, 96, 8, 2, 2), (256, 1024, 8, 2, 1)])
+def test_moe_units_fp8_block(mk, B, H, I, E, topk, nf):
+    """Weight-only FP8 experts (E4M3 codes, one scale per gate, up and down tensor of each expert):
+    router -> FP8 expert units -> combine with the down scales; the activations, out8 and x_res
+    equal the oracle's FP8 form (moe_experts_fp8: FP16-rounded activations, exact products, the
+    row-dot order, the scale on each row's total, BF16) bit for bit."""
+    from fleet.pack_weights import fp8_experts, quantize_e4m3, unit_parts
+    g = gen(47 + H)
+    ns = topk + nf
+    x = rnd_bf16(g, H)
+    w_norm = (1.0 + 0.5 * torch.randn(H, generator=g, device=DEV)).to(torch.bfloat16)
+    W_gate = rnd_bf16(g, E, H, std=0.05)
+    W13 = rnd_bf16(g, E + nf, 2 * I, H, std=0.02)
+    W2 = rnd_bf16(g, E + nf, H, I, std=0.02)
+    W13q, s13, W2Fq, s2 = fp8_experts(W13, W2)
+    W2q, _ = quantize_e4m3(W2, 1)
+    b = _router_bufs(E=E, NS=ns, H=H, L=1)
+    sums = torch.full((ns, unit_parts(I), 8, H), float("nan"), dtype=torch.float32, device=DEV)
+    act8 = torch.zeros(ns, I, dtype=torch.bfloat16, device=DEV)
+    out8 = torch.zeros(ns, H, dtype=torch.bfloat16, device=DEV)
+    x_res = x.clone()
+    tag = dict(logit_tag=torch.zeros(E, dtype=torch.int64, device=DEV),
+               mask_tag=torch.zeros(ns, dtype=torch.int64, device=DEV))
+    ops = [B.moe_router_layer(mk, None, x_res, w_norm, W_gate, b["h"], b["topk_w"], b["routing"], b["mask"],
+                              b["logits"], b["route_log"], layer_index=0, topk=topk, n_experts=E, n_forced=nf,
+                              scaling=1.0, eps=1e-6, **tag),
+           B.moe_units_layer(mk, None, x_res, W13q, W2Fq, sums, slot0=0, nslots=ns, inter=I, w_norm=w_norm,
+                             mask=b["mask"], act=act8, norm=True, fixed0=topk, static_experts=E,
+                             mask_tag=tag["mask_tag"], scale13=s13),
+           B.moe_combine_layer(mk, None, sums, b["topk_w"], x_res, x_res, inter=I, out8=out8, mask=b["mask"],
+                               scale2=s2)]
+    run_ops(mk, ops)
+    h, logits, topk_w, routing, mask = R.moe_router_norm(np32(x), np32(w_norm), np32(W_gate), topk=topk,
+                                                         n_experts=E, forced=tuple(range(E, E + nf)))
+    assert np.array_equal(b["mask"].cpu().numpy()[:ns], mask[:ns])
+    want_act, want_out8 = R.moe_experts_fp8(h, W13q.cpu().numpy(), s13.cpu().numpy(), W2q.cpu().numpy(),
+                                            s2.cpu().numpy(), mask, n_slots=ns)
+    assert_bits_equal(act8, want_act, "act")
+    assert_bits_equal(out8, want_out8, "out8")
+    assert_bits_equal(x_res, R.moe_combine(want_out8, topk_w, np32(x)), "combined x_res")
+
+
 def test_dense_mlp(mk, B):
     """Layer 0: norm2 + gate/up (+SwiGLU) over I 10,944, then the K-split down projection."""
     from fleet.pack_weights import REAL_DIMS as d

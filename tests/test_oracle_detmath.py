@@ -221,3 +221,62 @@ def test_c_mla_attend_equals_numpy(nh, dc, dr, s, pos, split):
     finally:
         D._OD_LIB = saved
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+# ---- FP8 (E4M3) experts ----------------------------------------------------------------------
+
+
+def test_e4m3_table_matches_torch():
+    """The oracle's E4M3 decoding (from the format's definition) equals torch.float8_e4m3fn on all
+    256 codes (NaN codes 0x7F and 0xFF included)."""
+    from oracle import numpy_ref as R
+    codes = torch.arange(256, dtype=torch.int32).to(torch.uint8)
+    want = codes.view(torch.float8_e4m3fn).float().numpy()
+    got = R.e4m3(np.arange(256))
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    ok = ~np.isnan(want)
+    assert np.array_equal(got[ok].view(np.uint32), want[ok].view(np.uint32))
+    assert R.e4m3(np.array([0x7E]))[0] == 448.0 and R.e4m3(np.array([0x01]))[0] == 2.0 ** -9
+
+
+def test_quantize_e4m3_scales_and_codes():
+    """Per-tensor scales amax / 448 (gate and up rows of the interleaved W13 apart); every code is a
+    finite E4M3 value; the largest weight of a tensor maps to +-448 and decoding times the scale
+    stays within half an E4M3 step of each weight; an all-zero tensor gets scale 1."""
+    from fleet.pack_weights import fp8_experts, quantize_e4m3, regroup_w2
+    from oracle import numpy_ref as R
+    g = torch.Generator().manual_seed(5)
+    W13 = (0.02 * torch.randn(3, 2 * 64, 96, generator=g)).to(torch.bfloat16)
+    W13[2] = 0
+    q, s = quantize_e4m3(W13, 2)
+    assert q.dtype == torch.uint8 and s.shape == (3, 2)
+    w = W13.float().numpy()
+    for e in range(2):
+        for p in range(2):
+            rows = w[e, p::2]
+            assert np.float32(s[e, p]) == np.float32(np.abs(rows).max() / np.float32(448.0))
+            dec = R.e4m3(q[e, p::2].numpy())
+            assert np.isfinite(dec).all() and np.abs(dec).max() == 448.0
+            err = np.abs(dec * s[e, p].item() - rows)
+            assert (err <= np.abs(rows) * 2.0 ** -4 + 2.0 ** -10 * s[e, p].item()).all()
+    assert s[2].tolist() == [1.0, 1.0] and int(q[2].sum()) == 0
+    W2 = (0.02 * torch.randn(3, 96, 64, generator=g)).to(torch.bfloat16)
+    W13q, s13, W2Fq, s2 = fp8_experts(W13, W2)
+    W2q, s2b = quantize_e4m3(W2, 1)
+    assert torch.equal(W13q, q) and torch.equal(s13, s) and torch.equal(s2, s2b.reshape(-1))
+    assert torch.equal(W2Fq, regroup_w2(W2q))
+
+
+def test_linear_fp8_is_exact_products_in_row_order():
+    """linear_fp8 = bf16(scale * dot_rows(e4m3(q), f16(x))): each product is exact (4 x 11
+    significant bits), so the dot is the row-dot order over exact products; close to the FP64 dot."""
+    from oracle import numpy_ref as R
+    rng = np.random.default_rng(9)
+    q = rng.integers(0, 256, size=(16, 1408), dtype=np.uint8)
+    q[(q & 0x7F) == 0x7F] = 0x00                                   # no NaN codes
+    x = R.bf16(rng.standard_normal(1408).astype(np.float32))
+    y = R.linear_fp8(x, q, np.float32(0.01))
+    xd = R.f16(x).astype(np.float64)
+    ref = 0.01 * (R.e4m3(q).astype(np.float64) @ xd)
+    assert np.allclose(y, ref, rtol=2e-2, atol=1e-2 * np.abs(ref).max())
+    assert np.array_equal(y, R.bf16((np.float32(0.01) * D.dot_rows(R.e4m3(q), R.f16(x))).astype(np.float32)))
