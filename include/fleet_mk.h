@@ -102,9 +102,10 @@ enum MkOpType {
 #define MK_F_FP8 (1 << 7)        /* MOE_UNITS / MOE_COMBINE: weight-only FP8 experts (the reference's D26):
                                     W13 and W2F hold E4M3 codes (one byte), one scale per tensor (gate,
                                     up and down of each expert); the activations are rounded to FP16
-                                    for the products, which are exact in FP32 (4 and 11 significant
-                                    bits), the sums run in the BF16 form's order, and each row's total
-                                    is multiplied by its tensor's scale before the BF16 rounding */
+                                    (finite values beyond it saturate at +-65504) for the products,
+                                    which are exact in FP32 (4 and 11 significant bits), the sums run
+                                    in the BF16 form's order, and each row's total is multiplied by its
+                                    tensor's scale before the BF16 rounding */
 
 #define MK_MAX_PTRS 16
 #define MK_MAX_IPARAMS 16

@@ -372,8 +372,12 @@ def e4m3(q):
 
 
 def f16(x):
-    """float32 values rounded to FP16 (nearest even) and back: the FP8 path's activation operand."""
-    return np.asarray(x, F32).astype(np.float16).astype(F32)
+    """float32 values rounded to FP16 (nearest even) and back, finite values beyond the FP16 range
+    saturated at +-65504: the FP8 path's activation operand."""
+    x = np.asarray(x, F32)
+    with np.errstate(over="ignore"):
+        y = x.astype(np.float16).astype(F32)
+    return np.where(np.isinf(y) & np.isfinite(x), np.copysign(F32(65504.0), x), y).astype(F32)
 
 
 def linear_fp8(x, Wq, scale):

@@ -405,22 +405,30 @@ def test_moe_units_block(mk, B, H, I, E, topk, nf, tags):
     assert_bits_equal(x_res, R.moe_combine(want_out8, topk_w, np32(x)), "combined x_res")
 
 
-@pytest.mark.parametrize("H,I,E,topk,nf", [(2048, 1408, 64, 6, 2), (64, 96, 8, 2, 2), (256, 1024, 8, 2, 1)])
-def test_moe_units_fp8_block(mk, B, H, I, E, topk, nf):
+@pytest.mark.parametrize("H,I,E,topk,nf,sat", [(2048, 1408, 64, 6, 2, False), (2048, 1408, 64, 6, 2, True),
+                                              (64, 96, 8, 2, 2, False), (256, 1024, 8, 2, 1, False)])
+def test_moe_units_fp8_block(mk, B, H, I, E, topk, nf, sat):
     """Weight-only FP8 experts (E4M3 codes, one scale per gate, up and down tensor of each expert):
     router -> FP8 expert units -> combine with the down scales; the activations, out8 and x_res
     equal the oracle's FP8 form (moe_experts_fp8: FP16-rounded activations, exact products, the
-    row-dot order, the scale on each row's total, BF16) bit for bit."""
+    row-dot order, the scale on each row's total, BF16) bit for bit. The codes include subnormal
+    E4M3 values (exponent field 0). sat: one normalised activation far beyond the FP16 range
+    (saturated at 65504 for the products, as the oracle's f16 does)."""
     from fleet.pack_weights import fp8_experts, quantize_e4m3, unit_parts
     g = gen(47 + H)
     ns = topk + nf
     x = rnd_bf16(g, H)
     w_norm = (1.0 + 0.5 * torch.randn(H, generator=g, device=DEV)).to(torch.bfloat16)
+    if sat:
+        w_norm[7] = 65536.0                 # h[7] ~ 65536 x[7] / rms(x), rms(x) ~ 1: >> 65504
+        x[7] = 4.0
     W_gate = rnd_bf16(g, E, H, std=0.05)
     W13 = rnd_bf16(g, E + nf, 2 * I, H, std=0.02)
     W2 = rnd_bf16(g, E + nf, H, I, std=0.02)
     W13q, s13, W2Fq, s2 = fp8_experts(W13, W2)
     W2q, _ = quantize_e4m3(W2, 1)
+    sub = ((W13q & 0x78) == 0) & ((W13q & 0x07) != 0)
+    assert bool(sub.any()) or H * I < 2 ** 16, "no subnormal codes"
     b = _router_bufs(E=E, NS=ns, H=H, L=1)
     sums = torch.full((ns, unit_parts(I), 8, H), float("nan"), dtype=torch.float32, device=DEV)
     act8 = torch.zeros(ns, I, dtype=torch.bfloat16, device=DEV)
@@ -439,6 +447,7 @@ def test_moe_units_fp8_block(mk, B, H, I, E, topk, nf):
     run_ops(mk, ops)
     h, logits, topk_w, routing, mask = R.moe_router_norm(np32(x), np32(w_norm), np32(W_gate), topk=topk,
                                                          n_experts=E, forced=tuple(range(E, E + nf)))
+    assert not sat or abs(h[7]) > 65504
     assert np.array_equal(b["mask"].cpu().numpy()[:ns], mask[:ns])
     want_act, want_out8 = R.moe_experts_fp8(h, W13q.cpu().numpy(), s13.cpu().numpy(), W2q.cpu().numpy(),
                                             s2.cpu().numpy(), mask, n_slots=ns)

@@ -280,3 +280,17 @@ def test_linear_fp8_is_exact_products_in_row_order():
     ref = 0.01 * (R.e4m3(q).astype(np.float64) @ xd)
     assert np.allclose(y, ref, rtol=2e-2, atol=1e-2 * np.abs(ref).max())
     assert np.array_equal(y, R.bf16((np.float32(0.01) * D.dot_rows(R.e4m3(q), R.f16(x))).astype(np.float32)))
+
+
+def test_f16_activation_rounding():
+    """The FP8 path's activation operand: exact for BF16 values of magnitude in [2^-14, 65504],
+    nearest-even below, saturated at +-65504 above (the kernel's cvt.rn.satfinite)."""
+    from oracle import numpy_ref as R
+    x = np.array([1.0, -3.5, 2.0 ** -14, 65504.0, 65536.0, -1e30, 2.0 ** -20 * 1.5, 2.0 ** -26, np.nan], np.float32)
+    y = R.f16(x)
+    assert y[:4].tolist() == [1.0, -3.5, 2.0 ** -14, 65504.0]
+    assert y[4] == 65504.0 and y[5] == -65504.0
+    assert y[6] == np.float32(np.float16(2.0 ** -20 * 1.5)) and y[7] == 0.0 and np.isnan(y[8])
+    b = R.bf16(np.random.default_rng(3).standard_normal(4096).astype(np.float32) * 100)
+    ok = (np.abs(b) >= 2.0 ** -14) & (np.abs(b) <= 65504)
+    assert np.array_equal(R.f16(b)[ok], b[ok])
