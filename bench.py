@@ -259,7 +259,8 @@ def time_steps(mpk, meta, steps, torch, stream):
 def trace_summary(mpk, plan, out=sys.stderr):
     """Per-operator breakdown of the last launch's trace (one token): for each operator of a middle
     layer its task count, the most tasks one CTA ran, and the median task's prologue (activations
-    loaded), stages (weights consumed) and epilogue (outputs, release); then, per operator kind,
+    loaded), stages (weights consumed), of which the consumers waited for a ring stage (wait), and
+    epilogue (outputs, release); then, per operator kind,
     the median over the middle layers of how much it extends the token's critical path (its last
     task's end minus the latest end of every operator before it)."""
     import statistics as st
@@ -267,14 +268,15 @@ def trace_summary(mpk, plan, out=sys.stderr):
     labels = [c.label for c in plan.calls]
     by = {}
     for (op, task, cta, it, t_ready, t_end, t_body, t_stages, wait) in recs:
-        by.setdefault(op, []).append((t_ready, t_end, t_body, t_stages, cta))
+        by.setdefault(op, []).append((t_ready, t_end, t_body, t_stages, cta, wait))
     if not by:
         return
     ends = {op: max(r[1] for r in v) for op, v in by.items()}
     layers = sorted({int(lb[1:].split(".")[0]) for lb in labels if lb.startswith("L")})
     mid = layers[len(layers) // 2] if layers else None
     print(f"trace of one token: operators of layer {mid} (us; medians over tasks)", file=out)
-    print("%-18s %6s %7s %8s %8s %8s" % ("operator", "tasks", "max/cta", "prologue", "stages", "epilogue"), file=out)
+    print("%-18s %6s %7s %8s %8s %8s %8s" % ("operator", "tasks", "max/cta", "prologue", "stages", "wait", "epilogue"),
+          file=out)
     for op in sorted(by):
         if not labels[op].startswith(f"L{mid}."):
             continue
@@ -285,7 +287,9 @@ def trace_summary(mpk, plan, out=sys.stderr):
         pro = st.median([(r[2] - r[0]) / 1e3 for r in v if r[2]]) if any(r[2] for r in v) else 0.0
         stg = st.median([(r[3] - r[2]) / 1e3 for r in v if r[3] and r[2]]) if any(r[3] for r in v) else 0.0
         epi = st.median([(r[1] - (r[3] or r[2] or r[0])) / 1e3 for r in v])
-        print("%-18s %6d %7d %8.2f %8.2f %8.2f" % (labels[op], len(v), max(per_cta.values()), pro, stg, epi), file=out)
+        wt = st.median([r[5] / 1e3 for r in v])
+        print("%-18s %6d %7d %8.2f %8.2f %8.2f %8.2f" % (labels[op], len(v), max(per_cta.values()), pro, stg, wt, epi),
+              file=out)
     order = sorted(by)
     kinds = {}
     for i in range(1, len(order)):
