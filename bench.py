@@ -397,19 +397,21 @@ def cpu_baseline(w, split, budget_s):
             "sample": dec.describe(len(times))}
 
 
-def roofline(d, ms_per_token, ctx, bw_peak, peak_kind, world=1, expert_bytes=2):
+def roofline(d, ms_per_token, ctx, bw_peak, peak_kind, world=1, expert_bytes=2, layers=None):
     """Algorithmic HBM bytes of one GPU's launch per token over its time: with expert parallelism
     rank 0 (the busiest) reads the replicated weights and the expert weights of ceil(N_SLOTS /
-    world) of the eight slots. expert_bytes: 1 for the FP8 experts."""
+    world) of the eight slots. expert_bytes: 1 for the FP8 experts. layers: the graph's layers
+    (the model's 27 by default); the committed traffic captures are of the 27-layer token."""
     from fleet.pack_weights import active_bytes_per_token, slot_bytes_per_token
-    algo = active_bytes_per_token(d, ctx=ctx, expert_bytes=expert_bytes)
+    layers = d.L if layers is None else layers
+    algo = active_bytes_per_token(d, ctx=ctx, layers=layers, expert_bytes=expert_bytes)
     if world > 1:
         mine = -(-d.N_SLOTS // world)
-        algo -= slot_bytes_per_token(d) * (d.N_SLOTS - mine)
+        algo -= slot_bytes_per_token(d, layers=layers) * (d.N_SLOTS - mine)
     achieved = algo / (ms_per_token * 1e-3) / 1e9
     traffic = None
-    f = ROOT / "profiles" / "decode_traffic.txt"
-    if f.exists() and world == 1 and expert_bytes == 2:   # the capture of the BF16 graph
+    f = ROOT / "profiles" / ("decode_traffic.txt" if expert_bytes == 2 else "decode_traffic_fp8.txt")
+    if f.exists() and world == 1 and layers == d.L:
         for line in f.read_text().splitlines():
             if line.startswith("traffic_bytes_per_token:"):
                 traffic = float(line.split(":", 1)[1])
@@ -479,7 +481,7 @@ def run_ours(args):
     bw, kind = peaks()
     ctx = ctx0 + args.steps // 2
     fp8 = plan.moe == "units_fp8"
-    roof = roofline(d, ms, ctx, bw, kind, ws, expert_bytes=1 if fp8 else 2)
+    roof = roofline(d, ms, ctx, bw, kind, ws, expert_bytes=1 if fp8 else 2, layers=args.layers)
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         try:
