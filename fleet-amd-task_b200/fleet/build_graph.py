@@ -444,10 +444,16 @@ def build(packed, capture, meta, dims=REAL_DIMS, s_max=1056, layers=27, head=Tru
             op.ntasks = int(op_tasks[kind])
         if c.beside and op.ntasks == 0:
             # the operators it runs beside keep their CTAs; it takes the rest (tasks are dealt to
-            # CTAs in chain order from a rotating start, so the free CTAs are the next ones)
+            # CTAs in chain order from a rotating start, so the free CTAs are the next ones). The
+            # expert units take every CTA: their last tasks, on the CTAs of the operators beside,
+            # run routed units only, after those operators (fleet_mk.h MK_I_MU_FTASKS)
             busy = sum(kernel.tasks(index[b]) for b in c.beside)
             if 0 < busy < n_cta:
-                op.ntasks = n_cta - busy
+                if c.method == "moe_units_layer":
+                    op.ntasks = n_cta
+                    op.ip[mk.P["mu_i"]["FTASKS"]] = n_cta - busy
+                else:
+                    op.ntasks = n_cta - busy
         kernel.add(op)
         index[c.label] = i
     set_plan_deps(plan, kernel)

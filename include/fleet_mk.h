@@ -184,6 +184,13 @@ enum { /* MK_OP_MOE_UNITS */ MK_P_MU_X = 0, MK_P_MU_WNORM = 1, MK_P_MU_W13 = 2, 
        MK_I_MU_H = 0, MK_I_MU_I = 1, MK_I_MU_SLOT0 = 2, MK_I_MU_NSLOTS = 3 /* slots of this operator */,
        MK_I_MU_NS = 4 /* all slots (SUMS, ACT) */, MK_I_MU_NEXP = 5, MK_I_MU_EXP0 = 6 /* MK_F_STATIC_IDS */,
        MK_I_MU_FIXED0 = 7 /* the first slot with a fixed expert (SLOT0 + NSLOTS: none) */,
+       MK_I_MU_FTASKS = 8 /* the tasks [0, FTASKS) share the fixed slots' units (0, or FTASKS at least
+                             the task count, which is at most the live units: every task); the
+                             others run routed units only (an operator beside the router gives its
+                             tasks on the router's CTAs no fixed units: they start when it is done).
+                             The operator's tasks are dealt to CTAs from the rotating start, so with
+                             one task per CTA the last tasks land on the CTAs of the operators just
+                             before it */,
        MK_P_MU_SCALE13 = 9 /* MK_F_FP8: [experts][2] FP32, the gate and up scales */ };
 /* MK_OP_MOE_COMBINE: per row r and slot s, the down projection's part sums
    ((S_0 + S_4) + (S_2 + S_6)) + ((S_1 + S_5) + (S_3 + S_7)) added in part order, rounded to BF16

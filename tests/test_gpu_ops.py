@@ -354,10 +354,13 @@ def test_moe_block(mk, B):
     assert_bits_equal(x_res, R.moe_combine(want_out8, topk_w, np32(x)), "combined x_res")
 
 
-@pytest.mark.parametrize("H,I,E,topk,nf,tags", [(2048, 1408, 64, 6, 2, True), (2048, 1408, 64, 6, 2, False),
-                                               (64, 96, 8, 2, 2, True), (128, 256, 12, 3, 1, False),
-                                               (256, 1024, 8, 2, 1, True)])
-def test_moe_units_block(mk, B, H, I, E, topk, nf, tags):
+@pytest.mark.parametrize("H,I,E,topk,nf,tags,beside", [(2048, 1408, 64, 6, 2, True, False),
+                                                      (2048, 1408, 64, 6, 2, True, True),
+                                                      (2048, 1408, 64, 6, 2, False, False),
+                                                      (64, 96, 8, 2, 2, True, False),
+                                                      (128, 256, 12, 3, 1, False, True),
+                                                      (256, 1024, 8, 2, 1, True, False)])
+def test_moe_units_block(mk, B, H, I, E, topk, nf, tags, beside):
     """The expert units: router -> the units of every slot (each task normalises x_res itself, runs
     its share of the shared slots' units with their fixed experts, then its share of the routed
     slots' units with the router's experts) -> the combine into x_res; out8, the
@@ -366,7 +369,8 @@ def test_moe_units_block(mk, B, H, I, E, topk, nf, tags):
     12 lanes in one part (classes of one and two lanes), 32 lanes in one part (four-lane classes)
     and 32 lanes in four parts. tags: the router hands its logits to its task 0 and the slots'
     experts to the units as tagged words (the decode graph's form), else through its arrival
-    counter and completion event."""
+    counter and completion event. beside: the units take one task per CTA and their last tasks, on
+    the router's CTAs, run routed units only (MK_I_MU_FTASKS, the decode graph's form)."""
     from fleet.pack_weights import unit_parts
     g = gen(43 + H)
     ns = topk + nf
@@ -392,6 +396,12 @@ def test_moe_units_block(mk, B, H, I, E, topk, nf, tags):
                              mask=b["mask"], act=act8, norm=True, fixed0=topk, static_experts=E,
                              mask_tag=tag.get("mask_tag")),
            B.moe_combine_layer(mk, None, sums, b["topk_w"], x_res, x_res, inter=I, out8=out8)]
+    if beside:
+        n_cta = torch.cuda.get_device_properties(0).multi_processor_count
+        n_rt = 8 if E % 8 == 0 else 4
+        ops[0].ntasks = n_rt
+        ops[1].ntasks = n_cta
+        ops[1].ip[mk.P["mu_i"]["FTASKS"]] = n_cta - n_rt
     run_ops(mk, ops)
     dw = DeviceWeights({"W13": W13, "W2": W2})
     h, logits, topk_w, routing, mask = R.moe_router_norm(np32(x), np32(w_norm), np32(W_gate), topk=topk,
