@@ -45,7 +45,9 @@ extern "C" {
 /* device status error codes (MkStatus.error) */
 #define MK_DERR_NONE 0
 #define MK_DERR_WAIT_TIMEOUT 1     /* an event wait ran past MkConfig.wait_timeout_ns */
-#define MK_DERR_RING_TIMEOUT 2     /* a weight-stream stage did not arrive / free in time */
+#define MK_DERR_RING_TIMEOUT 2     /* a weight-stream stage did not arrive / free in time (err_info 1:
+                                      a consumer's wait, 2: the producer's, 3: a leaving producer could
+                                      not drain its copies in flight; err_op and err_task are then ~0) */
 #define MK_DERR_TOKEN_RANGE 3      /* a token id outside [0, V) was read (clamped) */
 #define MK_DERR_ABORTED 4          /* another CTA reported an error first */
 #define MK_DERR_BAD_EXPERT 5       /* a routed expert id outside [0, E_TOTAL) */
