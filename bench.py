@@ -311,8 +311,9 @@ def trace_summary(mpk, plan, out=sys.stderr):
 
 
 def time_e2e(mpk, meta, steps, torch, stream):
-    """Through the public API with host buffers: per step the input token H2D from pinned memory,
-    one launch, the output token D2H to pinned memory."""
+    """Through the public API with host buffers (mpk.decode_token, the library's mk_decode_token):
+    per step the input token H2D from pinned memory, one launch, the output token D2H to pinned
+    memory, and the wait for it on the host."""
     tok_in = torch.zeros(1, dtype=torch.int64, pin_memory=True)
     tok_out = torch.zeros(1, dtype=torch.int64, pin_memory=True)
     tokens = meta["tokens"]
@@ -324,13 +325,7 @@ def time_e2e(mpk, meta, steps, torch, stream):
     e0.record(stream)
     t0 = time.perf_counter()
     for _ in range(steps):
-        pos = mpk.step + 1
-        with torch.cuda.stream(stream):
-            tokens[0, pos:pos + 1].copy_(tok_in, non_blocking=True)
-        mpk.launch(1, stream)
-        with torch.cuda.stream(stream):
-            tok_out.copy_(tokens[0, pos + 1:pos + 2], non_blocking=True)
-        stream.synchronize()
+        mpk.decode_token(tok_in, tok_out, stream)
         tok_in.copy_(tok_out)
     e1.record(stream)
     torch.cuda.synchronize()

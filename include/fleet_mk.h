@@ -265,6 +265,14 @@ int mk_finalize(MkHandle* h);
    and writes tokens[step + 2 + i]; `meta_step` (int32 device pointer or NULL) receives
    step + iters when the launch completes (the reference's prepare_next_batch, D14). */
 int mk_launch(MkHandle* h, void* stream, int32_t iters, int32_t step, int32_t* meta_step);
+/* One greedy token from host memory to host memory, in C (no per-token driver code between the
+   copies and the launch): *token_in (pinned host int64) is copied to tokens[step + 1] on the
+   device, one iteration runs at step (as mk_launch with iters 1), tokens[step + 2] is copied to
+   *token_out (pinned host int64), and the call returns when the stream is done. `tokens` is the
+   device int64 row the plan's embedding reads (meta tokens[0]). The host side of the reference's
+   greedy loop, harness/run_reference.py:380-398, one token per call. */
+int mk_decode_token(MkHandle* h, void* stream, int64_t* tokens, int32_t step, const int64_t* token_in,
+                    int64_t* token_out, int32_t* meta_step);
 /* Copy the device status word (synchronises the handle's last stream). MK_EDEVICE if error. */
 int mk_status(MkHandle* h, MkStatus* out);
 /* Clear a device error so the handle can launch again (the events are reset too). */

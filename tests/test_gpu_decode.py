@@ -122,6 +122,31 @@ def test_decode_launch_per_token_equals_one_launch():
     assert_bits_equal(host["logits"][0], rec["head.logits"], "logits")
 
 
+def test_decode_token_host_to_host():
+    """mk_decode_token (the end-to-end call): each step copies the host's token in, decodes one
+    token and copies it out; the host-fed greedy ids equal the oracle's. The device row holds no
+    token the host did not send (the prompt's last token is cleared there first)."""
+    layers, iters = 2, 3
+    d, packed, capture, meta, cache0, mpk, host, plan, pos0 = build_model(layers, iters, seed=7)
+    mpk.compile()
+    mpk.step = pos0 - 1
+    tok_in = torch.zeros(1, dtype=torch.int64, pin_memory=True)
+    tok_out = torch.zeros(1, dtype=torch.int64, pin_memory=True)
+    first = int(meta["tokens"][0, pos0].item())
+    tok_in.fill_(first)
+    meta["tokens"][0, pos0:] = -1
+    n_run = plan.s_max - 2 - (pos0 - 1)
+    ids = []
+    for _ in range(n_run):
+        mpk.decode_token(tok_in, tok_out)
+        ids.append(int(tok_out.item()))
+        tok_in.copy_(tok_out)
+    assert mpk.status()["error"] == 0
+    meta["tokens"][0, pos0] = first
+    want_ids, _, _, _ = oracle_run(d, packed, capture, meta, cache0, plan, layers, n_run, pos0)
+    assert ids == want_ids
+
+
 def test_decode_8k_context_matches_oracle():
     """Config 4's context on one GPU: 8,191 cached rows (seed 5), so every layer's attention runs
     65 splits of 128 rows per head and the merge combines all of them; a dense layer and a MoE
