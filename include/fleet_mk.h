@@ -263,7 +263,9 @@ int mk_finalize(MkHandle* h);
 /* Run `iters` decode iterations in ONE kernel launch on `stream` (a cudaStream_t, NULL for the
    default stream). Iteration i runs at position step + 1 + i: it reads tokens[step + 1 + i]
    and writes tokens[step + 2 + i]; `meta_step` (int32 device pointer or NULL) receives
-   step + iters when the launch completes (the reference's prepare_next_batch, D14). */
+   step + iters when the launch completes (the reference's prepare_next_batch, D14). MK_EINVAL if
+   a position falls outside the cache rows of the plan's mla_prep operators (step + iters + 1 >=
+   s_max) or step < -1: nothing is launched. */
 int mk_launch(MkHandle* h, void* stream, int32_t iters, int32_t step, int32_t* meta_step);
 /* One greedy token from host memory to host memory, in C (no per-token driver code between the
    copies and the launch): *token_in (pinned host int64) is copied to tokens[step + 1] on the

@@ -122,6 +122,24 @@ def test_decode_launch_per_token_equals_one_launch():
     assert_bits_equal(host["logits"][0], rec["head.logits"], "logits")
 
 
+def test_launch_rejects_positions_past_the_cache():
+    """A launch whose iterations would append cache rows or write tokens at s_max or beyond (or a
+    step below -1) is refused before anything runs; the handle still decodes afterwards."""
+    from fleet import mk
+    layers, iters = 2, 2
+    d, packed, capture, meta, cache0, mpk, host, plan, pos0 = build_model(layers, iters, seed=9)
+    mpk.compile()
+    for step, n in ((plan.s_max - 2, 1), (plan.s_max - 4, 3), (-2, 1)):
+        with pytest.raises(mk.MkError, match="s_max|step"):
+            mpk.kernel.launch(n, step)
+    tok = torch.zeros(1, dtype=torch.int64, pin_memory=True)
+    with pytest.raises(mk.MkError, match="s_max"):
+        mpk.kernel.decode_token(meta["tokens"][0], plan.s_max - 2, tok, tok)
+    mpk.step = pos0 - 1
+    mpk.launch(plan.s_max - 2 - (pos0 - 1))             # the last position is s_max - 1: allowed
+    assert mpk.status()["error"] == 0
+
+
 def test_decode_token_host_to_host():
     """mk_decode_token (the end-to-end call): each step copies the host's token in, decodes one
     token and copies it out; the host-fed greedy ids equal the oracle's. The device row holds no
